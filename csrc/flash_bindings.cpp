@@ -1,0 +1,120 @@
+// flash_bindings.cpp - torch surface of the tcgen05 flash forward (single GPU:
+// all K/V blocks already sit in local ring slots).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "flash.h"
+
+namespace rab {
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+Prec to_prec(int64_t p) {
+  TORCH_CHECK(p == 0 || p == 1, "prec must be 0 (bf16) or 1 (fp32 via 3xTF32)");
+  return static_cast<Prec>(p);
+}
+
+void ring_format(int64_t prec, torch::Tensor k, torch::Tensor v, torch::Tensor slot) {
+  const Prec pr = to_prec(prec);
+  TORCH_CHECK(k.is_cuda() && v.is_cuda() && slot.is_cuda(), "CUDA tensors required");
+  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && slot.is_contiguous(), "contiguous tensors");
+  TORCH_CHECK(k.dim() == 3 && v.sizes() == k.sizes(), "k/v must be [Skv, Hkv, D]");
+  TORCH_CHECK(k.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
+              "k/v dtype does not match prec");
+  const int Skv = k.size(0), Hkv = k.size(1), D = k.size(2);
+  const size_t need = ring_block_bytes(pr, Skv, Hkv, D);
+  TORCH_CHECK(static_cast<size_t>(slot.numel() * slot.element_size()) >= need, "slot too small");
+  const c10::cuda::CUDAGuard guard(k.device());
+  uint8_t* base = static_cast<uint8_t*>(slot.data_ptr());
+  const int err = ring_format_launch(pr, k.data_ptr(), v.data_ptr(), base,
+                                     base + ring_v_offset(pr, Skv, Hkv, D), Skv, Hkv, D,
+                                     cur_stream());
+  TORCH_CHECK(err == 0, "ring_format failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
+}
+
+std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slots, int64_t nblk,
+                               int64_t Skv, int64_t Hkv, c10::optional<torch::Tensor> out,
+                               c10::optional<torch::Tensor> lse, double scale, bool causal,
+                               bool zigzag, int64_t world, int64_t rank, int64_t nsplit,
+                               c10::optional<torch::Tensor> acc, c10::optional<torch::Tensor> m,
+                               c10::optional<torch::Tensor> l, torch::Tensor status,
+                               double timeout_s, int64_t grid) {
+  const Prec pr = to_prec(prec);
+  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.dim() == 3, "q must be contiguous [Sq, Hq, D]");
+  TORCH_CHECK(q.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
+              "q dtype does not match prec");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 8,
+              "status must be int32[8] on the GPU");
+  const c10::cuda::CUDAGuard guard(q.device());
+  FlashArgs a;
+  a.prec = pr;
+  a.q = q.data_ptr();
+  a.Sq = q.size(0);
+  a.Hq = q.size(1);
+  a.D = q.size(2);
+  a.Hkv = static_cast<int>(Hkv);
+  a.Skv = static_cast<int>(Skv);
+  a.nblk = static_cast<int>(nblk);
+  a.scale = static_cast<float>(scale);
+  const size_t bb = ring_block_bytes(pr, a.Skv, a.Hkv, a.D);
+  TORCH_CHECK(static_cast<size_t>(slots.numel() * slots.element_size()) >= bb * nblk,
+              "slots tensor too small for nblk blocks");
+  uint8_t* base = static_cast<uint8_t*>(slots.data_ptr());
+  a.k_base = base;
+  a.v_base = base + ring_v_offset(pr, a.Skv, a.Hkv, a.D);
+  a.slot_stride = bb;
+  a.causal = causal;
+  a.zigzag = zigzag;
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.nsplit = static_cast<int>(nsplit);
+  a.grid = static_cast<int>(grid);
+  a.status = reinterpret_cast<DeviceStatus*>(status.data_ptr());
+  a.timeout_s = timeout_s;
+  if (acc.has_value()) {
+    a.partial = true;
+    a.acc = acc->data_ptr<float>();
+    a.m = m ? m->data_ptr<float>() : nullptr;
+    a.l = l ? l->data_ptr<float>() : nullptr;
+  } else {
+    TORCH_CHECK(out.has_value(), "out (or partial acc/m/l) is required");
+    a.out = out->data_ptr();
+    a.out_bf16 = out->scalar_type() == torch::kBFloat16;
+    a.lse = lse ? lse->data_ptr<float>() : nullptr;
+  }
+  const FlashPlan pl = flash_plan(a);
+  torch::Tensor ws;
+  if (pl.workspace_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(pl.workspace_bytes)},
+                      torch::dtype(torch::kUInt8).device(q.device()));
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = pl.workspace_bytes;
+  }
+  const int err = flash_run(a, pl, cur_stream());
+  TORCH_CHECK(err == 0, "flash_fwd launch failed: ",
+              cudaGetErrorString(static_cast<cudaError_t>(err)));
+  return {pl.nsplit, pl.n_items, pl.grid};
+}
+
+}  // namespace
+}  // namespace rab
+
+void register_flash(pybind11::module_& m) {
+  m.def("ring_block_bytes", [](int64_t prec, int64_t Skv, int64_t Hkv, int64_t D) {
+    return static_cast<int64_t>(rab::ring_block_bytes(static_cast<rab::Prec>(prec), Skv, Hkv, D));
+  });
+  m.def("ring_v_offset", [](int64_t prec, int64_t Skv, int64_t Hkv, int64_t D) {
+    return static_cast<int64_t>(rab::ring_v_offset(static_cast<rab::Prec>(prec), Skv, Hkv, D));
+  });
+  m.def("ring_format", &rab::ring_format, "write one K/V block into a ring slot");
+  m.def("flash_fwd", &rab::flash_fwd, "tcgen05 flash attention over local ring slots",
+        py::arg("prec"), py::arg("q"), py::arg("slots"), py::arg("nblk"), py::arg("Skv"),
+        py::arg("Hkv"), py::arg("out") = c10::nullopt, py::arg("lse") = c10::nullopt,
+        py::arg("scale") = 1.0, py::arg("causal") = false, py::arg("zigzag") = false,
+        py::arg("world") = 1, py::arg("rank") = 0, py::arg("nsplit") = 0,
+        py::arg("acc") = c10::nullopt, py::arg("m") = c10::nullopt, py::arg("l") = c10::nullopt,
+        py::arg("status"), py::arg("timeout_s") = 10.0, py::arg("grid") = 0);
+  m.def("sm_count", &rab::flash_sm_count);
+}

@@ -1,0 +1,74 @@
+// status.h - device status word shared by every kernel that waits on anything.
+//
+// Waits in this code base are bounded: when a wait runs out it records an error
+// code, the wait site and the block/rank that gave up, then the kernel unwinds
+// normally.  The host reads the word after the launch and raises a clean error;
+// the CUDA context stays usable.  No kernel traps.
+#pragma once
+
+#include <cstdint>
+
+namespace rab {
+
+enum StatusCode : uint32_t {
+  kStatusOk = 0,
+  kStatusTimeout = 1,     // a bounded wait ran out
+  kStatusBadArgs = 2,     // device-side argument check failed
+  kStatusBounds = 3,      // DEBUG_BOUNDS index check failed
+  kStatusPeerError = 4,   // a peer rank published an error flag
+};
+
+// Wait-site identifiers (reported as `where`).
+enum WaitSite : uint32_t {
+  kSiteNone = 0,
+  kSiteQFull = 1,
+  kSiteKFull = 2,
+  kSiteVFull = 3,
+  kSiteKEmpty = 4,
+  kSiteVEmpty = 5,
+  kSiteSFull = 6,
+  kSitePFull = 7,
+  kSiteOReady = 8,
+  kSiteBlockReady = 9,     // waiting for a ring block to land in local memory
+  kSitePeerReady = 10,     // waiting for a peer's published epoch
+  kSitePeerConsumed = 11,  // waiting for peers to finish reading our buffers
+  kSiteCopySlice = 12,
+  kSiteRingFlag = 13,      // comm-only ring copy flag
+  kSiteTest = 14,          // deliberately unsatisfiable wait used by tests
+  kSitePvDone = 15,
+};
+
+struct DeviceStatus {
+  uint32_t code;       // StatusCode, first error wins
+  uint32_t where;      // WaitSite of the first error
+  uint32_t block;      // blockIdx.x that recorded it
+  uint32_t detail;     // site-specific (step, tile, peer...)
+  uint32_t n_errors;   // how many threads/blocks hit an error
+  uint32_t pad[3];
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t st_read_error(DeviceStatus* st) {
+  if (st == nullptr) return 0;
+  return *reinterpret_cast<volatile uint32_t*>(&st->code);
+}
+
+__device__ __forceinline__ void st_record(DeviceStatus* st, uint32_t code, uint32_t where,
+                                          uint32_t detail = 0) {
+  if (st == nullptr) return;
+  atomicAdd(&st->n_errors, 1u);
+  if (atomicCAS(&st->code, 0u, code) == 0u) {
+    st->where = where;
+    st->block = blockIdx.x;
+    st->detail = detail;
+    __threadfence_system();
+  }
+}
+
+__device__ __forceinline__ void st_record_timeout(DeviceStatus* st, uint32_t where,
+                                                  uint32_t detail = 0) {
+  st_record(st, kStatusTimeout, where, detail);
+}
+#endif
+
+}  // namespace rab

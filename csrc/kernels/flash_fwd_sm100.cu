@@ -1,0 +1,923 @@
+// flash_fwd_sm100.cu - tcgen05 flash-attention forward for B200 (sm_100a),
+// optionally fused with the ring: while the tensor cores consume the K/V blocks
+// already in local memory, two copy warps in every CTA pull the blocks of the
+// other ranks over NVLink (peer-mapped loads, 16-byte vectors) into this rank's
+// ring slots.  Online softmax state stays on chip across all ring steps, so the
+// per-step merge of the reference (src/attention/ring_attention_nccl_gpu_bench.cu
+// :341-348, kernels C16 + C17) disappears into the running rescale.
+//
+// CTA = 8 warps, one 128-row query tile of one head at a time (persistent over
+// work items):
+//   warp 0      TMA producer: K / V tiles of the ring slots -> shared memory
+//   warp 1      MMA issuer (one thread): S = Q K^T and O += P V on tcgen05,
+//               commits to mbarriers; also owns the TMEM allocation
+//   warps 2-3   ring copy warps (fused mode): peer slot -> local slot
+//   warps 4-7   softmax: one thread per query row; S and O live in TMEM,
+//               P is written back over S (A operand of the PV MMA from TMEM)
+//
+// Precisions:
+//   kBF16   bf16 Q/K/V, kind::f16, fp32 accumulation, bf16 P.
+//   kF32x3  fp32 Q/K/V.  Every product is formed as three kind::tf32 MMAs on
+//           tf32 big/small splits (a_b*b_b + a_b*b_s + a_s*b_b; Ootomo &
+//           Yokota 2022), P included, which keeps fp32-level accuracy on the
+//           tensor cores.  Q is split in the kernel; K and V^T arrive pre-split
+//           in the ring slots.
+//
+// The softmax uses lazy rescaling: the running max only moves (and O is only
+// rescaled in TMEM) when a row max grows by more than 2^8, which keeps the
+// exponentials <= 256 and the result exact up to rounding.
+//
+// Every wait is bounded (globaltimer); a timeout records the wait site in the
+// status word and the CTA unwinds (draining its own TMA loads and MMAs) instead
+// of hanging.  No TMA load here uses cluster multicast.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "flash.h"
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace rab {
+
+using namespace sm100;
+
+namespace {
+
+constexpr int kM = 128;
+constexpr int kThreads = 256;
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpComm = 2;      // warps 2 and 3
+constexpr int kWarpSoftmax = 4;   // warps 4..7
+constexpr float kRescaleThreshold = 8.0f;
+constexpr float kLn2 = 0.69314718055994530942f;
+constexpr uint32_t kTmemCols = 512;
+
+template <Prec P, int D>
+struct Cfg {
+  static constexpr bool kTF32 = (P == Prec::kF32x3);
+  static_assert(!kTF32 || D == 64, "3xTF32 path supports head_dim 64");
+  static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
+  static constexpr int kN = kTF32 ? 64 : 128;       // keys per tile
+  static constexpr int kEsize = kTF32 ? 4 : 2;
+  static constexpr int kElems128 = 128 / kEsize;    // elements in a 128-byte row
+  static constexpr int kPlanes = kTF32 ? 2 : 1;
+  static constexpr int kKTile = kN * D * kEsize * kPlanes;  // bytes
+  static constexpr int kVTile = kKTile;
+  static constexpr int kStages = (kKTile + kVTile) <= 32768 ? 4 : 3;
+  static constexpr int kSmemTiles = kStages * (kKTile + kVTile);
+  static constexpr int kNumBars = 4 * kStages + 8;
+  static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
+  // TMEM columns
+  static constexpr uint32_t kColQ = 0;                       // Q (tf32: Qb at 0, Qs at D)
+  static constexpr uint32_t kQCols = kTF32 ? D : D / 2;      // per plane (tf32 only uses it)
+  static constexpr uint32_t kColS0 = 128;
+  static constexpr uint32_t kColS1 = kColS0 + (kTF32 ? 64 : 128);
+  static constexpr uint32_t kColPs0 = kTF32 ? 256 : 0;       // tf32 small P planes
+  static constexpr uint32_t kColPs1 = kTF32 ? 320 : 0;
+  static constexpr uint32_t kColO = 384;
+  // K-steps (each tcgen05.mma consumes 32 bytes of K)
+  static constexpr int kKStepsQK = D * kEsize / 32;
+  static constexpr int kKStepsPV = kN * kEsize / 32;
+  static constexpr uint32_t kIdescQK =
+      make_idesc(kTF32 ? kFmtTF32 : kFmtBF16, kTF32 ? kFmtTF32 : kFmtBF16, kM, kN, kMajorK, kMajorK);
+  static constexpr uint32_t kIdescPV = make_idesc(kTF32 ? kFmtTF32 : kFmtBF16,
+                                                  kTF32 ? kFmtTF32 : kFmtBF16, kM, D, kMajorK,
+                                                  kTF32 ? kMajorK : kMajorMN);
+};
+
+struct Item {
+  int unit, chunk, h, hk, q0, v_begin, v_end;
+};
+
+__device__ __forceinline__ Item make_item(const FlashParams& p, int item, int tiles_total) {
+  Item it;
+  it.chunk = item / p.n_units;
+  it.unit = item - it.chunk * p.n_units;
+  it.h = it.unit % p.Hq;
+  const int qt = it.unit / p.Hq;
+  it.hk = it.h / (p.Hq / p.Hkv);
+  it.q0 = qt * kM;
+  it.v_begin = static_cast<int>(static_cast<long long>(it.chunk) * tiles_total / p.nsplit);
+  it.v_end = static_cast<int>(static_cast<long long>(it.chunk + 1) * tiles_total / p.nsplit);
+  return it;
+}
+
+__device__ __forceinline__ int global_pos(int local, int owner, int S, int W, int zigzag) {
+  if (!zigzag) return owner * S + local;
+  const int C = S >> 1;
+  return local < C ? owner * C + local : (2 * W - 1 - owner) * C + (local - C);
+}
+
+// Tile classification: 0 = skip (fully masked), 1 = full, 2 = diagonal (mask per element)
+__device__ __forceinline__ int classify(const FlashParams& p, const Item& it, int v, int kN,
+                                        int tpb, int* k_lo_out, int* q_lo_out) {
+  if (!p.causal) return 1;
+  const int s = v / tpb, t = v - (v / tpb) * tpb;
+  const int owner = ((p.rank - s) % p.world + p.world) % p.world;
+  const int q_lo = global_pos(it.q0, p.rank, p.Sq, p.world, p.zigzag);
+  const int q_hi = q_lo + kM - 1;
+  const int k_lo = global_pos(t * kN, owner, p.Skv, p.world, p.zigzag);
+  const int k_hi = k_lo + kN - 1;
+  *k_lo_out = k_lo;
+  *q_lo_out = q_lo;
+  if (k_lo > q_hi) return 0;
+  if (k_hi <= q_lo) return 1;
+  return 2;
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Bounded poll of a 64-bit flag until it reaches `target`.
+__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, bool sys,
+                                          DeviceStatus* st, uint32_t where, uint32_t detail,
+                                          uint64_t timeout_ns) {
+  if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
+    if (st_read_error(st) != 0) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      st_record_timeout(st, where, detail);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+template <Prec P, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_kernel(const __grid_constant__ FlashParams p, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV) {
+  using C = Cfg<P, D>;
+  constexpr int kN = C::kN;
+  constexpr int NS = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + NS * C::kKTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemTiles);
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = bars + NS;
+  uint64_t* v_full = bars + 2 * NS;
+  uint64_t* v_empty = bars + 3 * NS;
+  uint64_t* s_full = bars + 4 * NS;       // [2]
+  uint64_t* p_full = bars + 4 * NS + 2;   // [2]
+  uint64_t* pv_done = bars + 4 * NS + 4;
+  uint64_t* q_full = bars + 4 * NS + 5;
+  uint64_t* o_final = bars + 4 * NS + 6;
+  uint64_t* drain = bars + 4 * NS + 7;
+  __shared__ uint32_t tmem_slot;
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  DeviceStatus* st = p.status;
+  const uint64_t tmo = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
+    mbar_init(pv_done, 1);
+    mbar_init(q_full, 128);
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  const int tpb = p.Skv / kN;                 // tiles per block
+  const int tiles_total = p.nblk * tpb;
+
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------------ TMA
+    if (elect_one()) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int g = 0;
+      int ready_blocks = 1;  // blocks [0, ready_blocks) known present locally
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
+        const Item it = make_item(p, item, tiles_total);
+        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
+          int k_lo, q_lo;
+          if (classify(p, it, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          const int s = v / tpb, t = v - s * tpb;
+          if (p.fused && s >= ready_blocks) {
+            ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
+                           kSiteBlockReady, s, tmo);
+            if (!ok) break;
+            fence_proxy_async_global();
+            ready_blocks = s + 1;
+          }
+          const int stage = g % NS;
+          const uint32_t ph = (g / NS) & 1;
+          ok = mbar_wait(&k_empty[stage], ph ^ 1, st, kSiteKEmpty, tmo);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&k_full[stage], C::kKTile);
+          uint8_t* kdst = sK + stage * C::kKTile;
+          if constexpr (C::kTF32) {
+#pragma unroll
+            for (int ds = 0; ds < D / C::kElems128; ++ds)
+              tma_load_5d(kdst + ds * (2 * kN * 128), &tmK, &k_full[stage], ds * C::kElems128,
+                          it.hk, t * kN, 0, s);
+          } else {
+#pragma unroll
+            for (int ds = 0; ds < D / C::kElems128; ++ds)
+              tma_load_4d(kdst + ds * (kN * 128), &tmK, &k_full[stage], ds * C::kElems128, it.hk,
+                          t * kN, s);
+          }
+          ok = mbar_wait(&v_empty[stage], ph ^ 1, st, kSiteVEmpty, tmo);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&v_full[stage], C::kVTile);
+          uint8_t* vdst = sV + stage * C::kVTile;
+          if constexpr (C::kTF32) {
+#pragma unroll
+            for (int ks = 0; ks < kN / C::kElems128; ++ks)
+              tma_load_5d(vdst + ks * (2 * D * 128), &tmV, &v_full[stage],
+                          t * kN + ks * C::kElems128, 0, it.hk, 0, s);
+          } else {
+#pragma unroll
+            for (int ds = 0; ds < D / C::kElems128; ++ds)
+              tma_load_4d(vdst + ds * (kN * 128), &tmV, &v_full[stage], ds * C::kElems128, it.hk,
+                          t * kN, s);
+          }
+          ++g;
+        }
+      }
+      if (!ok) {
+        // drain the loads this thread issued before giving up
+        for (int i = 0; i < NS && i < g; ++i) {
+          const int gg = g - 1 - i;
+          const int stage = gg % NS;
+          const uint32_t ph = (gg / NS) & 1;
+          mbar_wait(&k_full[stage], ph, nullptr, kSiteKFull, 100000000ull);
+          mbar_wait(&v_full[stage], ph, nullptr, kSiteVFull, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------------ MMA
+    if (elect_one()) {
+      int g = 0;
+      int item_count = 0;
+      int final_count = 0;  // items that had at least one visible tile
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
+        const Item it = make_item(p, item, tiles_total);
+        ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
+        if (!ok) break;
+        tc_fence_after();
+        int j = 0;
+        auto issue_pv = [&](int gp, bool first) -> bool {
+          const int b = gp & 1;
+          const int stage = gp % NS;
+          if (!mbar_wait(&p_full[b], (gp >> 1) & 1, st, kSitePFull, tmo)) return false;
+          if (!mbar_wait(&v_full[stage], (gp / NS) & 1, st, kSiteVFull, tmo)) return false;
+          tc_fence_after();
+          const uint32_t vbase = smem_u32(sV + stage * C::kVTile);
+          const uint32_t d_tm = tmem + C::kColO;
+          if constexpr (C::kTF32) {
+            const uint32_t pb = tmem + (b ? C::kColS1 : C::kColS0);
+            const uint32_t ps = tmem + (b ? C::kColPs1 : C::kColPs0);
+            // passes: (Ps, Vb), (Pb, Vs), (Pb, Vb); V^T planes: b at +0, s at +D*128
+#pragma unroll
+            for (int pass = 0; pass < 3; ++pass) {
+              const uint32_t a_col = pass == 0 ? ps : pb;
+              const uint32_t plane = pass == 1 ? D * 128 : 0;
+#pragma unroll
+              for (int ks = 0; ks < C::kKStepsPV; ++ks) {
+                const uint32_t sub = ks >> 2, inner = (ks & 3) * 32;
+                const uint64_t bdesc =
+                    make_sdesc(vbase + sub * (2 * D * 128) + plane + inner, 16, 1024);
+                const uint32_t acc = (first && pass == 0 && ks == 0) ? 0u : 1u;
+                mma_ts<true>(d_tm, a_col + ks * 8, bdesc, C::kIdescPV, acc);
+              }
+            }
+          } else {
+            const uint32_t pa = tmem + (b ? C::kColS1 : C::kColS0);
+#pragma unroll
+            for (int ks = 0; ks < C::kKStepsPV; ++ks) {
+              // MN-major V: 16 keys (2 x 8-row atoms) per step; 64-wide d blocks at LBO
+              const uint64_t bdesc = make_sdesc(vbase + ks * 2048, kN * 128, 1024);
+              const uint32_t acc = (first && ks == 0) ? 0u : 1u;
+              mma_ts<false>(d_tm, pa + ks * 8, bdesc, C::kIdescPV, acc);
+            }
+          }
+          mma_commit(&v_empty[stage]);
+          mma_commit(pv_done);
+          return true;
+        };
+        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
+          int k_lo, q_lo;
+          if (classify(p, it, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          const int stage = g % NS;
+          const int b = g & 1;
+          ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t kbase = smem_u32(sK + stage * C::kKTile);
+          const uint32_t s_tm = tmem + (b ? C::kColS1 : C::kColS0);
+          if constexpr (C::kTF32) {
+            // passes: (Qs, Kb), (Qb, Ks), (Qb, Kb); K planes: b at +0, s at +kN*128
+#pragma unroll
+            for (int pass = 0; pass < 3; ++pass) {
+              const uint32_t a_col = tmem + C::kColQ + (pass == 0 ? C::kQCols : 0);
+              const uint32_t plane = pass == 1 ? kN * 128 : 0;
+#pragma unroll
+              for (int ks = 0; ks < C::kKStepsQK; ++ks) {
+                const uint32_t sub = ks >> 2, inner = (ks & 3) * 32;
+                const uint64_t bdesc =
+                    make_sdesc(kbase + sub * (2 * kN * 128) + plane + inner, 16, 1024);
+                mma_ts<true>(s_tm, a_col + ks * 8, bdesc, C::kIdescQK,
+                             (pass == 0 && ks == 0) ? 0u : 1u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < C::kKStepsQK; ++ks) {
+              const uint32_t sub = ks >> 2, inner = (ks & 3) * 32;
+              const uint64_t bdesc = make_sdesc(kbase + sub * (kN * 128) + inner, 16, 1024);
+              mma_ts<false>(s_tm, tmem + C::kColQ + ks * 8, bdesc, C::kIdescQK, ks ? 1u : 0u);
+            }
+          }
+          mma_commit(&s_full[b]);
+          mma_commit(&k_empty[stage]);
+          if (j > 0) ok = issue_pv(g - 1, j == 1);
+          ++j;
+          ++g;
+        }
+        if (ok && j > 0) {
+          ok = issue_pv(g - 1, j == 1);
+          if (ok) mma_commit(o_final);
+          ++final_count;
+        }
+      }
+      // make sure nothing of ours is still running before TMEM is released
+      mma_commit(drain);
+      mbar_wait(drain, 0, nullptr, kSiteOReady, 1000000000ull);
+    }
+  } else if (warp == kWarpComm || warp == kWarpComm + 1) {
+    // ------------------------------------------------------------ ring copy
+    if (p.fused && p.world > 1) {
+      const int ct = threadIdx.x - kWarpComm * 32;  // 0..63
+      if (blockIdx.x == 0 && ct == 0)
+        st_release_sys(p.flags_local + kFlagSlot0Ready, p.epoch);
+      const int left = (p.rank - 1 + p.world) % p.world;
+      const size_t n16 = p.slot_bytes / 16;
+      const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
+      const size_t beg = per * blockIdx.x;
+      const size_t end = beg + per < n16 ? beg + per : n16;
+      bool ok = true;
+      for (int s = 1; s < p.nblk && ok; ++s) {
+        const uint4* src;
+        uint64_t* src_flags;
+        if (p.ring_chain) {
+          src = reinterpret_cast<const uint4*>(p.peer_slots[left] + (size_t)(s - 1) * p.slot_bytes);
+          src_flags = p.flags_peer[left];
+          if (ct == 0) {
+            ok = (s == 1) ? wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st,
+                                      kSitePeerReady, left, tmo)
+                          : wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true,
+                                      st, kSitePeerReady, left, tmo);
+          }
+        } else {
+          const int origin = ((p.rank - s) % p.world + p.world) % p.world;
+          src = reinterpret_cast<const uint4*>(p.peer_slots[origin]);
+          src_flags = p.flags_peer[origin];
+          if (ct == 0)
+            ok = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, origin,
+                           tmo);
+        }
+        named_bar_sync(1, 64);
+        ok = st_read_error(st) == 0;
+        if (!ok) break;
+        uint4* dst = reinterpret_cast<uint4*>(p.local_slots + (size_t)s * p.slot_bytes);
+        size_t i = beg + ct;
+        constexpr int U = 8;
+        for (; i + (U - 1) * 64 < end; i += U * 64) {
+          uint4 r[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) r[u] = __ldcg(src + i + u * 64);
+#pragma unroll
+          for (int u = 0; u < U; ++u) __stcg(dst + i + u * 64, r[u]);
+        }
+        for (; i < end; i += 64) __stcg(dst + i, __ldcg(src + i));
+        fence_proxy_async_global();
+        __threadfence_system();
+        named_bar_sync(1, 64);
+        if (ct == 0) {
+          red_add_release_sys(p.flags_local + kFlagArrivedBase + s, 1);
+          red_add_release_sys(src_flags + kFlagReads, 1);
+        }
+      }
+      // this rank's slots must outlive every peer's reads of this launch
+      if (ok && blockIdx.x == 0 && ct == 0)
+        wait_flag(p.flags_local + kFlagReads, p.reads_target, true, st, kSitePeerConsumed, 0,
+                  tmo);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int row = threadIdx.x - kWarpSoftmax * 32;   // 0..127, TMEM lane
+    const uint32_t wq = warp & 3;                      // TMEM sub-partition
+    const uint32_t lane_base = (wq * 32) << 16;
+    const float sl2 = p.scale_log2;
+    int g = 0;
+    int item_count = 0;
+    int final_count = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
+      const Item it = make_item(p, item, tiles_total);
+      const int qrow = it.q0 + row;
+      // ---- Q -> TMEM ----
+      {
+        if constexpr (C::kTF32) {
+          const float4* qp = reinterpret_cast<const float4*>(
+              static_cast<const float*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D);
+          uint32_t big[32], small[32];
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = __ldg(qp + c / 4 + i);
+              split_tf32(x.x, big[4 * i + 0], small[4 * i + 0]);
+              split_tf32(x.y, big[4 * i + 1], small[4 * i + 1]);
+              split_tf32(x.z, big[4 * i + 2], small[4 * i + 2]);
+              split_tf32(x.w, big[4 * i + 3], small[4 * i + 3]);
+            }
+            tmem_st32(tmem + lane_base + C::kColQ + c, big);
+            tmem_st32(tmem + lane_base + C::kColQ + C::kQCols + c, small);
+          }
+        } else {
+          const uint4* qp = reinterpret_cast<const uint4*>(
+              static_cast<const uint16_t*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D);
+          uint32_t w[32];
+#pragma unroll
+          for (int c = 0; c < D / 2; c += 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint4 x = __ldg(qp + c / 4 + i);
+              w[4 * i + 0] = x.x;
+              w[4 * i + 1] = x.y;
+              w[4 * i + 2] = x.z;
+              w[4 * i + 3] = x.w;
+            }
+            tmem_st32(tmem + lane_base + C::kColQ + c, w);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(q_full);
+      }
+      float m_run = -INFINITY;  // running max of scaled log2 scores
+      float l_run = 0.f;
+      int j = 0;
+      for (int v = it.v_begin; v < it.v_end && ok; ++v) {
+        int k_lo = 0, q_lo = 0;
+        const int cls = classify(p, it, v, kN, tpb, &k_lo, &q_lo);
+        if (cls == 0) continue;
+        const int b = g & 1;
+        ok = mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t s_tm = tmem + lane_base + (b ? C::kColS1 : C::kColS0);
+        uint32_t sr[kN];
+#pragma unroll
+        for (int c = 0; c < kN; c += 32) tmem_ld32(s_tm + c, sr + c);
+        tmem_ld_wait();
+        if (cls == 2) {
+          const int lim = q_lo + row - k_lo;  // key index c visible iff c <= lim
+#pragma unroll
+          for (int c = 0; c < kN; ++c)
+            if (c > lim) sr[c] = 0xff800000u;  // -inf
+        }
+        float mx = __uint_as_float(sr[0]);
+#pragma unroll
+        for (int c = 1; c < kN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        mx *= sl2;
+        // lazy rescale: move the reference max only when it grows by > 2^8
+        const bool need = mx > m_run + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - mx);
+          m_run = mx;
+          l_run *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // O holds PV of earlier tiles: wait until the last PV landed, then scale rows
+          ok = mbar_wait(pv_done, (g - 1) & 1, st, kSitePvDone, tmo);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t o_tm = tmem + lane_base + C::kColO;
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(o_tm + c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_tm + c, o);
+          }
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        float rowsum = 0.f;
+        if constexpr (C::kTF32) {
+          uint32_t pb[32], ps[32];
+#pragma unroll
+          for (int c = 0; c < kN; c += 32) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e = ex2_approx(fmaf(__uint_as_float(sr[c + i]), sl2, -m_use));
+              rowsum += e;
+              split_tf32(e, pb[i], ps[i]);
+            }
+            tmem_st32(s_tm + c, pb);
+            tmem_st32(tmem + lane_base + (b ? C::kColPs1 : C::kColPs0) + c, ps);
+          }
+        } else {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < kN; c += 64) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i]), sl2, -m_use));
+              const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i + 1]), sl2, -m_use));
+              rowsum += e0 + e1;
+              pk[i] = pack_bf16x2(e0, e1);
+            }
+            tmem_st32(s_tm + c / 2, pk);
+          }
+        }
+        l_run += rowsum;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[b]);
+        ++j;
+        ++g;
+      }
+      if (!ok) break;
+      // ---- epilogue ----
+      const bool have = j > 0;
+      if (have) {
+        ok = mbar_wait(o_final, final_count & 1, st, kSiteOReady, tmo);
+        ++final_count;
+        if (!ok) break;
+        tc_fence_after();
+      }
+      const uint32_t o_tm = tmem + lane_base + C::kColO;
+      const float m_nat = have ? m_run * kLn2 : -INFINITY;
+      const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
+      const bool split = p.nsplit > 1;
+      const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
+      float* dst_f32 = nullptr;
+      if (split)
+        dst_f32 = p.split_acc + (static_cast<size_t>(item) * kM + row) * D;
+      else if (p.partial)
+        dst_f32 = p.acc + r * D;
+      else if (!p.out_bf16)
+        dst_f32 = static_cast<float*>(p.out) + r * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        if (have) {
+          tmem_ld32(o_tm + c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (dst_f32 != nullptr) {
+          float4* d4 = reinterpret_cast<float4*>(dst_f32 + c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                __uint_as_float(o[4 * i + 2]) * inv,
+                                __uint_as_float(o[4 * i + 3]) * inv);
+        } else {
+          uint4* d4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + r * D + c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv,
+                                           __uint_as_float(o[8 * i + 1]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv,
+                                           __uint_as_float(o[8 * i + 3]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv,
+                                           __uint_as_float(o[8 * i + 5]) * inv),
+                               pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv,
+                                           __uint_as_float(o[8 * i + 7]) * inv));
+        }
+      }
+      if (split) {
+        p.split_m[static_cast<size_t>(item) * kM + row] = m_nat;
+        p.split_l[static_cast<size_t>(item) * kM + row] = l_run;
+      } else if (p.partial) {
+        if (p.m_out) p.m_out[r] = m_nat;
+        if (p.l_out) p.l_out[r] = l_run;
+      } else if (p.lse != nullptr) {
+        p.lse[r] = (have && l_run > 0.f) ? m_nat + logf(l_run) : -INFINITY;
+      }
+      // all TMEM reads of this item are done before the next Q lands in TMEM
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// split merge: combine nsplit partials of each unit
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void split_merge_kernel(const FlashParams p) {
+  constexpr int kTpr = D / 4;
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long rows_total = static_cast<long long>(p.n_units) * kM;
+  const long long urow = t / kTpr;
+  const int c = static_cast<int>(t % kTpr);
+  if (urow >= rows_total) return;
+  const int unit = static_cast<int>(urow / kM);
+  const int row = static_cast<int>(urow % kM);
+  const int h = unit % p.Hq;
+  const int qrow = (unit / p.Hq) * kM + row;
+  float mx = -INFINITY;
+  for (int k = 0; k < p.nsplit; ++k)
+    mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * kM + row]);
+  const float mref = (mx == -INFINITY) ? 0.f : mx;
+  float l = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < p.nsplit; ++k) {
+    const size_t it = static_cast<size_t>(k) * p.n_units + unit;
+    const float mk = p.split_m[it * kM + row];
+    const float w = (mk == -INFINITY) ? 0.f : expf(mk - mref);
+    l += w * p.split_l[it * kM + row];
+    const float4 x = reinterpret_cast<const float4*>(p.split_acc + (it * kM + row) * D)[c];
+    a.x += w * x.x;
+    a.y += w * x.y;
+    a.z += w * x.z;
+    a.w += w * x.w;
+  }
+  const size_t r = static_cast<size_t>(qrow) * p.Hq + h;
+  if (p.partial) {
+    reinterpret_cast<float4*>(p.acc + r * D)[c] = a;
+    if (c == 0) {
+      if (p.m_out) p.m_out[r] = mx;
+      if (p.l_out) p.l_out[r] = l;
+    }
+    return;
+  }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  a.x *= inv;
+  a.y *= inv;
+  a.z *= inv;
+  a.w *= inv;
+  if (p.out_bf16) {
+    uint2 pk;
+    pk.x = pack_bf16x2(a.x, a.y);
+    pk.y = pack_bf16x2(a.z, a.w);
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + r * D)[c] = pk;
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(p.out) + r * D)[c] = a;
+  }
+  if (c == 0 && p.lse != nullptr) p.lse[r] = l > 0.f ? mx + logf(l) : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------
+// ring-format preparation (3xTF32): K -> planes, V -> transposed planes
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tf32_pair(float x, float& b, float& s) {
+  uint32_t bb, ss;
+  split_tf32(x, bb, ss);
+  b = __uint_as_float(bb);
+  s = __uint_as_float(ss);
+}
+
+__global__ void split_k_kernel(const float4* __restrict__ k, float4* __restrict__ kb,
+                               float4* __restrict__ ks, size_t n4) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 x = k[i];
+    float4 b, s;
+    tf32_pair(x.x, b.x, s.x);
+    tf32_pair(x.y, b.y, s.y);
+    tf32_pair(x.z, b.z, s.z);
+    tf32_pair(x.w, b.w, s.w);
+    kb[i] = b;
+    ks[i] = s;
+  }
+}
+
+// V [Skv][Hkv][D] -> VT planes [2][Hkv][D][Skv]; 32x32 tiles through shared memory.
+__global__ void split_vt_kernel(const float* __restrict__ v, float* __restrict__ vt, int Skv,
+                                int Hkv, int D) {
+  __shared__ float tile[32][33];
+  const int hk = blockIdx.z;
+  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y)
+    tile[i][threadIdx.x] = v[(static_cast<size_t>(s0 + i) * Hkv + hk) * D + d0 + threadIdx.x];
+  __syncthreads();
+  const size_t plane = static_cast<size_t>(Hkv) * D * Skv;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    float b, s;
+    tf32_pair(tile[threadIdx.x][i], b, s);
+    const size_t o = (static_cast<size_t>(hk) * D + d0 + i) * Skv + s0 + threadIdx.x;
+    vt[o] = b;
+    vt[plane + o] = s;
+  }
+}
+
+template <Prec P, int D>
+void set_smem_attr() {
+  using C = Cfg<P, D>;
+  cudaFuncSetAttribute(flash_fwd_kernel<P, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       C::kSmemBytes);
+}
+
+template <Prec P, int D>
+int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
+                cudaStream_t stream) {
+  using C = Cfg<P, D>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    set_smem_attr<P, D>();
+    attr_done = true;
+  }
+  if (p.Skv % C::kN != 0)
+    throw std::runtime_error("flash: keys per block must be a multiple of " +
+                             std::to_string(C::kN));
+  if (cooperative) {
+    void* args[] = {const_cast<FlashParams*>(&p), const_cast<CUtensorMap*>(&maps.k),
+                    const_cast<CUtensorMap*>(&maps.v)};
+    return static_cast<int>(cudaLaunchCooperativeKernel(
+        reinterpret_cast<void*>(flash_fwd_kernel<P, D>), dim3(grid), dim3(kThreads), args,
+        C::kSmemBytes, stream));
+  }
+  flash_fwd_kernel<P, D><<<grid, kThreads, C::kSmemBytes, stream>>>(p, maps.k, maps.v);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+int flash_sm_count() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+size_t ring_v_offset(Prec prec, int Skv, int Hkv, int D) {
+  const size_t e = static_cast<size_t>(Skv) * Hkv * D;
+  const size_t k_bytes = prec == Prec::kF32x3 ? 2 * e * 4 : e * 2;
+  return (k_bytes + 1023) / 1024 * 1024;
+}
+
+size_t ring_block_bytes(Prec prec, int Skv, int Hkv, int D) {
+  const size_t e = static_cast<size_t>(Skv) * Hkv * D;
+  const size_t v_bytes = prec == Prec::kF32x3 ? 2 * e * 4 : e * 2;
+  return (ring_v_offset(prec, Skv, Hkv, D) + v_bytes + 4095) / 4096 * 4096;
+}
+
+FlashMaps flash_make_maps(Prec prec, const void* k_base, const void* v_base, size_t slot_stride,
+                          int nblk, int Skv, int Hkv, int D) {
+  FlashMaps m;
+  if (slot_stride == 0) slot_stride = ring_block_bytes(prec, Skv, Hkv, D);
+  if (prec == Prec::kF32x3) {
+    const uint64_t kn = 64;
+    {
+      uint64_t dims[5] = {(uint64_t)D, (uint64_t)Hkv, (uint64_t)Skv, 2, (uint64_t)nblk};
+      uint64_t strides[4] = {(uint64_t)D * 4, (uint64_t)Hkv * D * 4, (uint64_t)Skv * Hkv * D * 4,
+                             slot_stride};
+      uint32_t box[5] = {32, 1, (uint32_t)kn, 2, 1};
+      m.k = make_tmap(k_base, TmapDtype::kF32, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    {
+      uint64_t dims[5] = {(uint64_t)Skv, (uint64_t)D, (uint64_t)Hkv, 2, (uint64_t)nblk};
+      uint64_t strides[4] = {(uint64_t)Skv * 4, (uint64_t)D * Skv * 4,
+                             (uint64_t)Hkv * D * Skv * 4, slot_stride};
+      uint32_t box[5] = {32, (uint32_t)D, 1, 2, 1};
+      m.v = make_tmap(v_base, TmapDtype::kF32, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+  } else {
+    uint64_t dims[4] = {(uint64_t)D, (uint64_t)Hkv, (uint64_t)Skv, (uint64_t)nblk};
+    uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)Hkv * D * 2, slot_stride};
+    uint32_t box[4] = {64, 1, 128, 1};
+    m.k = make_tmap(k_base, TmapDtype::kBF16, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    m.v = make_tmap(v_base, TmapDtype::kBF16, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  return m;
+}
+
+int flash_choose_split(int units, int tiles_per_unit, int sms) {
+  int best = 1;
+  double best_eff = 0.0;
+  for (int c = 1; c <= 16; ++c) {
+    if (c > 1 && tiles_per_unit / c < 4) break;  // keep chunks long enough
+    const long long items = static_cast<long long>(units) * c;
+    const long long waves = (items + sms - 1) / sms;
+    const double eff = static_cast<double>(items) / static_cast<double>(waves * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = c;
+    }
+  }
+  return best;
+}
+
+int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps, int grid,
+                         bool cooperative, cudaStream_t stream) {
+  if (p.Sq % kM != 0) throw std::runtime_error("flash: query rows must be a multiple of 128");
+  if (p.Hq % p.Hkv != 0) throw std::runtime_error("flash: Hq must be a multiple of Hkv");
+  if (p.nblk > kMaxSlots) throw std::runtime_error("flash: too many blocks");
+  if (p.causal && p.zigzag && (p.Sq != p.Skv || (p.Sq / 2) % kM != 0))
+    throw std::runtime_error("flash: zigzag causal needs Sq == Skv and Sq/2 a multiple of 128");
+  if (prec == Prec::kF32x3) {
+    if (p.D != 64) throw std::runtime_error("flash: fp32 (3xTF32) path supports head_dim 64");
+    return launch_impl<Prec::kF32x3, 64>(p, maps, grid, cooperative, stream);
+  }
+  if (p.D == 64) return launch_impl<Prec::kBF16, 64>(p, maps, grid, cooperative, stream);
+  if (p.D == 128) return launch_impl<Prec::kBF16, 128>(p, maps, grid, cooperative, stream);
+  throw std::runtime_error("flash: head_dim must be 64 or 128");
+}
+
+int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream) {
+  const long long threads_total = static_cast<long long>(p.n_units) * kM * (p.D / 4);
+  const int bs = 256;
+  const int blocks = static_cast<int>((threads_total + bs - 1) / bs);
+  if (p.D == 64)
+    split_merge_kernel<64><<<blocks, bs, 0, stream>>>(p);
+  else
+    split_merge_kernel<128><<<blocks, bs, 0, stream>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int ring_format_launch(Prec prec, const void* k, const void* v, void* k_dst, void* v_dst, int Skv,
+                       int Hkv, int D, cudaStream_t stream) {
+  const size_t e = static_cast<size_t>(Skv) * Hkv * D;
+  if (prec == Prec::kBF16) {
+    cudaError_t err = cudaMemcpyAsync(k_dst, k, e * 2, cudaMemcpyDeviceToDevice, stream);
+    if (err == cudaSuccess)
+      err = cudaMemcpyAsync(v_dst, v, e * 2, cudaMemcpyDeviceToDevice, stream);
+    return static_cast<int>(err);
+  }
+  if (Skv % 32 != 0 || D % 32 != 0) throw std::runtime_error("ring_format: Skv, D % 32");
+  const size_t n4 = e / 4;
+  int blocks = static_cast<int>((n4 + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  float* kb = static_cast<float*>(k_dst);
+  split_k_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float4*>(k),
+                                             reinterpret_cast<float4*>(kb),
+                                             reinterpret_cast<float4*>(kb + e), n4);
+  dim3 g2(Skv / 32, D / 32, Hkv), b2(32, 8);
+  split_vt_kernel<<<g2, b2, 0, stream>>>(static_cast<const float*>(v), static_cast<float*>(v_dst),
+                                         Skv, Hkv, D);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace rab

@@ -1,0 +1,108 @@
+// flash_host.cpp - host planning of the flash forward: work split, grid,
+// workspace and cached tensor maps.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <tuple>
+
+#include "flash.h"
+
+namespace rab {
+
+namespace {
+
+using MapKey = std::tuple<int, const void*, const void*, size_t, int, int, int, int, int>;
+
+const FlashMaps& cached_maps(Prec prec, const void* k, const void* v, size_t stride, int nblk,
+                             int Skv, int Hkv, int D) {
+  static std::mutex mu;
+  static std::map<MapKey, FlashMaps> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key{static_cast<int>(prec), k, v, stride, nblk, Skv, Hkv, D, dev};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 256) cache.clear();
+  return cache.emplace(key, flash_make_maps(prec, k, v, stride, nblk, Skv, Hkv, D)).first->second;
+}
+
+}  // namespace
+
+FlashPlan flash_plan(const FlashArgs& a) {
+  if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
+  FlashPlan pl;
+  const int kN = a.prec == Prec::kF32x3 ? 64 : 128;
+  pl.n_units = a.Hq * (a.Sq / 128);
+  const int tiles = a.nblk * (a.Skv / kN);
+  const int sms = flash_sm_count();
+  pl.nsplit = a.nsplit > 0 ? a.nsplit : flash_choose_split(pl.n_units, tiles, sms);
+  if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;
+  pl.n_items = pl.n_units * pl.nsplit;
+  pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
+  if (a.fused) pl.grid = a.grid > 0 ? a.grid : sms;  // every CTA also copies a slice
+  pl.workspace_bytes =
+      pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * 128 * (a.D + 2) * sizeof(float) : 0;
+  return pl;
+}
+
+int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
+  if (pl.nsplit > 1 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace_bytes))
+    throw std::runtime_error("flash: split workspace missing or too small");
+  FlashParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = a.q;
+  p.Sq = a.Sq;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.D = a.D;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.nblk = a.nblk;
+  p.Skv = a.Skv;
+  p.causal = a.causal;
+  p.zigzag = a.zigzag;
+  p.world = a.world;
+  p.rank = a.rank;
+  p.nsplit = pl.nsplit;
+  p.n_units = pl.n_units;
+  p.n_items = pl.n_items;
+  p.out = a.out;
+  p.out_bf16 = a.out_bf16 ? 1 : 0;
+  p.lse = a.lse;
+  p.partial = a.partial ? 1 : 0;
+  p.acc = a.acc;
+  p.m_out = a.m;
+  p.l_out = a.l;
+  if (pl.nsplit > 1) {
+    float* ws = static_cast<float*>(a.workspace);
+    p.split_acc = ws;
+    p.split_m = ws + static_cast<size_t>(pl.n_items) * 128 * a.D;
+    p.split_l = p.split_m + static_cast<size_t>(pl.n_items) * 128;
+  }
+  p.fused = a.fused ? 1 : 0;
+  p.ring_chain = a.ring_chain ? 1 : 0;
+  p.local_slots = a.local_slots;
+  for (int r = 0; r < kMaxRanks; ++r) {
+    p.peer_slots[r] = a.peer_slots[r];
+    p.flags_peer[r] = a.flags_peer[r];
+  }
+  p.flags_local = a.flags_local;
+  p.slot_bytes = a.slot_bytes;
+  p.epoch = a.epoch;
+  p.arrive_target = a.arrive_target;
+  p.reads_target = a.reads_target;
+  p.status = a.status;
+  p.timeout_ns = static_cast<uint64_t>(a.timeout_s * 1e9);
+  if (p.status == nullptr) throw std::runtime_error("flash: a device status word is required");
+  const FlashMaps& maps =
+      cached_maps(a.prec, a.k_base, a.v_base, a.slot_stride, a.nblk, a.Skv, a.Hkv, a.D);
+  int err = flash_forward_launch(a.prec, p, maps, pl.grid, a.fused, stream);
+  if (err != 0) return err;
+  if (pl.nsplit > 1) err = flash_split_merge_launch(p, stream);
+  return err;
+}
+
+}  // namespace rab
