@@ -1,0 +1,228 @@
+#!/usr/bin/env python3
+"""Headline benchmark: fused ring attention on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the reference's full ring attention at its largest ATTENTION_SIZES
+entry, with N(0,1) data): every rank holds a 1,048,576-element K/V block laid
+out as [16384 tokens, 1 head, d=64] plus Q of the same shape, fp32, i.i.d.
+N(0,1) with seed = rank, softmax scale 1/sqrt(64), non-causal.  One step is one
+full ring-attention forward over all N blocks (N*16384 keys) on every rank,
+through the `b200_fused` engine: one persistent tcgen05 kernel per rank pulls
+the other ranks' blocks over NVLink while it computes.  Per-rank work grows
+with N (weak scaling in tokens per rank).
+
+Timing: W untimed warm-up steps; then K steps, each preceded by an L2 flush
+(a 256 MiB buffer write, outside the timed interval) and a host barrier, timed
+with CUDA events on the launching stream; the step time is the max over ranks,
+and the K-step loop is bracketed by a barrier plus torch.cuda.synchronize().
+value = total attention FLOPs of all ranks / max-rank step time.  The e2e
+number runs the same steps through the public `RingAttention` call with the
+inputs copied host->device from pinned memory and the output read back every
+step.  nvidia-smi samples the clocks during the timed loop.
+
+With --gpus N > 1 the script expects torchrun (RANK/WORLD_SIZE/LOCAL_RANK); run
+directly it re-launches itself on N local ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQ_PER_RANK = 16384
+HEADS = 1
+HEAD_DIM = 64
+METRIC = "ring_attention_fwd_tflops"
+L2_FLUSH_BYTES = 256 << 20
+REFERENCE_UNAVAILABLE = (
+    "the reference is a set of MPI programs (every source includes <mpi.h>) with no Python "
+    "package; pip cannot install it (no setup.py/pyproject.toml) and this image has no MPI "
+    "(no mpicxx, mpi.h or libmpi), so its binaries cannot be built or run")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--seq", type=int, default=SEQ_PER_RANK, help="tokens per rank")
+    ap.add_argument("--dtype", choices=("fp32", "bf16"), default="fp32")
+    ap.add_argument("--ring-mode", choices=("direct", "chain"), default="direct")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def reference_arm(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+    return 0
+
+
+def relaunch(args) -> int:
+    from ring_attention_benchmark_b200.launch import launch
+
+    return launch(args.gpus, [sys.executable] + sys.argv, timeout=1800)
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        return relaunch(args)
+    if args.warmup < 3:
+        print("bench.py: at least 3 warm-up steps are required", file=sys.stderr)
+        return 2
+
+    import torch
+
+    from ring_attention_benchmark_b200 import RingAttention
+    from ring_attention_benchmark_b200.models import inputs
+    from ring_attention_benchmark_b200.models.oracle import attention_flops
+    from ring_attention_benchmark_b200.utils.clocks import ClockSampler
+
+    attn = RingAttention(args.seq, HEADS, HEAD_DIM,
+                         dtype=torch.float32 if args.dtype == "fp32" else torch.bfloat16,
+                         ring_mode=args.ring_mode)
+    rt = attn.runtime
+    world, rank = rt.world, rt.rank
+    if world != args.gpus:
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+        return 2
+    dev = torch.device("cuda", rt.device)
+    dtype = attn.dtype
+    x = inputs.normal_inputs(rank, args.seq, HEADS, HEAD_DIM)
+    q = x.q.to(dev, dtype).contiguous()
+    k = x.k.to(dev, dtype).contiguous()
+    v = x.v.to(dev, dtype).contiguous()
+    out = torch.empty_like(q)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    flops_rank = attention_flops(args.seq, args.seq * world, HEADS, HEAD_DIM)
+    flops_total = flops_rank * world
+
+    # ---- warm-up ----
+    for _ in range(args.warmup):
+        attn(q, k, v, out=out)
+    attn.check()
+
+    # ---- device-timed steps ----
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(gpus=[rt.device] if world == 1 else None)
+    torch.cuda.synchronize(dev)
+    rt.barrier()
+    if rank == 0:
+        sampler.start()
+    t_wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize(dev)
+        rt.barrier()
+        starts[i].record(stream)
+        attn(q, k, v, out=out)
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    rt.barrier()
+    wall_ms = (time.perf_counter() - t_wall0) * 1e3
+    clocks = sampler.stop() if rank == 0 else None
+    attn.check()
+    local = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    step_max = []
+    for c in range(0, len(local), 16):
+        step_max += rt.reduce_max(local[c:c + 16])
+    ms_per_step = statistics.mean(step_max)
+    value = flops_total / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the public call: H2D inputs, D2H output ----
+    e2e = None
+    if not args.no_e2e:
+        q_h = x.q.to(dtype).pin_memory()
+        k_h = x.k.to(dtype).pin_memory()
+        v_h = x.v.to(dtype).pin_memory()
+        out_h = torch.empty(q.shape, dtype=dtype).pin_memory()
+        qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.warmup + args.steps):
+            flush.fill_(i & 0xFF)
+            torch.cuda.synchronize(dev)
+            rt.barrier()
+            j = i - args.warmup
+            if j >= 0:
+                e_s[j].record(stream)
+            qd.copy_(q_h, non_blocking=True)
+            kd.copy_(k_h, non_blocking=True)
+            vd.copy_(v_h, non_blocking=True)
+            o = attn(qd, kd, vd)
+            out_h.copy_(o, non_blocking=True)
+            if j >= 0:
+                e_e[j].record(stream)
+        torch.cuda.synchronize(dev)
+        attn.check()
+        loc = [s.elapsed_time(e) for s, e in zip(e_s, e_e)]
+        mx = []
+        for c in range(0, len(loc), 16):
+            mx += rt.reduce_max(loc[c:c + 16])
+        e2e_ms = statistics.mean(mx)
+        ok = bool(torch.isfinite(out_h).all())
+        e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": int((q_h.numel() + k_h.numel() + v_h.numel())
+                                         * q_h.element_size()),
+               "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()),
+               "output_finite": ok}
+
+    nsplit = attn.engine.nsplit
+    per_step = (2 if args.dtype == "fp32" else 0) + 1 + (1 if nsplit > 1 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp32" if args.dtype == "fp32" else "bf16",
+            "data": "synthetic",
+            "config": {
+                "model": f"ring attention fwd, {HEADS} head, d={HEAD_DIM}, non-causal, "
+                         f"{'fp32 via 3xTF32 tensor-core products' if args.dtype == 'fp32' else 'bf16'}",
+                "global_batch": 1,
+                "seq_len": args.seq * world,
+                "seq_per_rank": args.seq,
+                "kv_block_elements_per_rank": args.seq * HEADS * HEAD_DIM,
+                "parallelism": f"cp{world} (ring over NVLink, fused in-kernel transfer, "
+                               f"{args.ring_mode} mode)",
+                "data_init": "iid N(0,1), seed=rank, scale 1/sqrt(64)",
+                "l2": "256 MiB buffer written between timed steps (outside the events)",
+                "flops_per_step_total": flops_total,
+                "wall_ms_bracketed_loop": round(wall_ms, 3),
+                "nsplit": nsplit,
+                "grid": attn.engine.grid,
+            },
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    attn.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -41,6 +41,7 @@ struct FlashParams {
   int causal;           // 0/1
   int zigzag;           // 1: rank r holds global chunks r and 2W-1-r; 0: contiguous shards
   int world, rank;
+  int blk_offset;       // block s holds the keys of rank (rank - blk_offset - s) mod world
   // ---- work split ----
   int nsplit;           // KV chunks per (head, q tile) unit
   int n_units;          // heads * q tiles
@@ -121,6 +122,7 @@ struct FlashArgs {
   size_t slot_stride = 0;            // bytes between consecutive blocks
   int nblk = 1, Skv = 0;
   int causal = 0, zigzag = 0, world = 1, rank = 0;
+  int blk_offset = 0;                // first block is ring step blk_offset
   void* out = nullptr;
   bool out_bf16 = false;
   float* lse = nullptr;

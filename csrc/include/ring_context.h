@@ -77,6 +77,11 @@ class RingContext {
   // advances them identically (same launches in the same order).
   uint64_t next_epoch() { return ++epoch_; }
   uint64_t epoch() const { return epoch_; }
+  // Collective: zero every rank's device flag words and host transport words
+  // and restart all sequence counters (all ranks must call it together).
+  void reset_flags();
+  uint64_t next_xfer() { return ++xfer_seq_; }
+
   uint64_t take_steps(uint64_t n) {
     const uint64_t b = step_seq_;
     step_seq_ += n;
@@ -98,6 +103,7 @@ class RingContext {
   DeviceStatus* status_dev_ = nullptr;
   uint64_t epoch_ = 0;
   uint64_t step_seq_ = 0;
+  uint64_t xfer_seq_ = 0;
 };
 
 }  // namespace rab

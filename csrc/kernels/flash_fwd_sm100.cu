@@ -120,7 +120,7 @@ __device__ __forceinline__ int classify(const FlashParams& p, const Item& it, in
                                         int tpb, int* k_lo_out, int* q_lo_out) {
   if (!p.causal) return 1;
   const int s = v / tpb, t = v - (v / tpb) * tpb;
-  const int owner = ((p.rank - s) % p.world + p.world) % p.world;
+  const int owner = ((p.rank - p.blk_offset - s) % p.world + p.world) % p.world;
   const int q_lo = global_pos(it.q0, p.rank, p.Sq, p.world, p.zigzag);
   const int q_hi = q_lo + kM - 1;
   const int k_lo = global_pos(t * kN, owner, p.Skv, p.world, p.zigzag);

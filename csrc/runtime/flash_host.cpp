@@ -66,6 +66,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.zigzag = a.zigzag;
   p.world = a.world;
   p.rank = a.rank;
+  p.blk_offset = a.blk_offset;
   p.nsplit = pl.nsplit;
   p.n_units = pl.n_units;
   p.n_items = pl.n_items;

@@ -1,0 +1,113 @@
+// fused_ring.cpp - host side of the `b200_fused` ring attention engine.
+#include <sstream>
+#include <stdexcept>
+
+#include "drivers.h"
+
+namespace rab {
+
+size_t FusedRing::arena_bytes(Prec prec, int seq, int heads_kv, int dim, int world) {
+  return static_cast<size_t>(world) * ring_block_bytes(prec, seq, heads_kv, dim) + 4096;
+}
+
+FusedRing::FusedRing(RingContext& ctx, Prec prec, int seq, int heads, int heads_kv, int dim,
+                     bool causal, bool zigzag, bool ring_chain, double timeout_s)
+    : ctx_(ctx) {
+  const int np = ctx.world();
+  if (np > kMaxSlots) throw std::runtime_error("FusedRing: too many ranks");
+  if (np > 1 && !ctx.peers_open())
+    throw std::runtime_error("FusedRing: peer buffers must be mapped first");
+  if (np > 1 && !ctx.devices_unique())
+    throw std::runtime_error(
+        "FusedRing: ranks spin on each other inside the kernel and need one GPU each");
+  // the flag words count launches of this engine from zero on every rank
+  ctx.reset_flags();
+  slot_bytes_ = ring_block_bytes(prec, seq, heads_kv, dim);
+  slots_off_ = ctx.arena_alloc(static_cast<size_t>(np) * slot_bytes_, 4096);
+  FlashArgs& a = args_;
+  a.prec = prec;
+  a.Sq = seq;
+  a.Hq = heads;
+  a.Hkv = heads_kv;
+  a.D = dim;
+  a.Skv = seq;
+  a.nblk = np;
+  a.causal = causal ? 1 : 0;
+  a.zigzag = zigzag ? 1 : 0;
+  a.world = np;
+  a.rank = ctx.rank();
+  a.k_base = ctx.local(slots_off_);
+  a.v_base = ctx.local(slots_off_ + ring_v_offset(prec, seq, heads_kv, dim));
+  a.slot_stride = slot_bytes_;
+  a.status = ctx.status_dev();
+  a.timeout_s = timeout_s;
+  a.fused = np > 1;
+  a.ring_chain = ring_chain;
+  a.local_slots = ctx.local(slots_off_);
+  a.slot_bytes = slot_bytes_;
+  a.flags_local = ctx.flags_local();
+  for (int r = 0; r < np; ++r) {
+    a.peer_slots[r] = np > 1 ? ctx.peer(r, slots_off_) : ctx.local(slots_off_);
+    a.flags_peer[r] = np > 1 ? ctx.flags_peer(r) : ctx.flags_local();
+  }
+  plan_ = flash_plan(a);
+  if (plan_.workspace_bytes > 0)
+    cuda_check(cudaMalloc(&workspace_, plan_.workspace_bytes), "cudaMalloc(workspace)");
+  a.workspace = workspace_;
+  a.workspace_bytes = plan_.workspace_bytes;
+}
+
+FusedRing::~FusedRing() {
+  if (workspace_) cudaFree(workspace_);
+}
+
+uint8_t* FusedRing::slot0_k() const { return ctx_.local(slots_off_); }
+uint8_t* FusedRing::slot0_v() const {
+  return ctx_.local(slots_off_ + ring_v_offset(args_.prec, args_.Skv, args_.Hkv, args_.D));
+}
+
+void FusedRing::prepare(const void* k, const void* v, cudaStream_t stream) {
+  if (k == slot0_k() && v == slot0_v() && args_.prec == Prec::kBF16) return;
+  const int err = ring_format_launch(args_.prec, k, v, slot0_k(), slot0_v(), args_.Skv, args_.Hkv,
+                                     args_.D, stream);
+  cuda_check(static_cast<cudaError_t>(err), "ring_format");
+}
+
+void FusedRing::attend(const void* q, void* out, bool out_bf16, float* lse, float scale,
+                       cudaStream_t stream) {
+  FlashArgs a = args_;
+  a.q = q;
+  a.out = out;
+  a.out_bf16 = out_bf16;
+  a.lse = lse;
+  a.scale = scale;
+  if (a.fused) {
+    ++epoch_;
+    arrive_total_ += static_cast<uint64_t>(plan_.grid);
+    reads_total_ += static_cast<uint64_t>(a.world - 1) * plan_.grid;
+    a.epoch = epoch_;
+    a.arrive_target = arrive_total_;
+    a.reads_target = reads_total_;
+  }
+  const int err = flash_run(a, plan_, stream);
+  cuda_check(static_cast<cudaError_t>(err), "fused ring attention launch");
+}
+
+void FusedRing::forward(const void* q, const void* k, const void* v, void* out, bool out_bf16,
+                        float* lse, float scale, cudaStream_t stream) {
+  prepare(k, v, stream);
+  attend(q, out, out_bf16, lse, scale, stream);
+}
+
+void FusedRing::check() {
+  const DeviceStatus s = ctx_.read_status(true);
+  if (s.code != 0) {
+    std::ostringstream os;
+    os << "rank " << ctx_.rank() << ": fused ring attention wait timed out (site " << s.where
+       << ", block " << s.block << ", detail " << s.detail << ")";
+    ctx_.host().abort(os.str());
+    throw RankFailure(os.str());
+  }
+}
+
+}  // namespace rab

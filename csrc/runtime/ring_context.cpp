@@ -111,6 +111,21 @@ void RingContext::init_nccl(const std::string& uid) {
   nccl_check(ncclCommInitRank(&nccl_, world_, id, rank_), "ncclCommInitRank");
 }
 
+void RingContext::reset_flags() {
+  // every rank's kernels (which may write into peers' flags) finish first
+  cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+  cuda_check(cudaDeviceSynchronize(), "reset_flags sync");
+  host_->barrier();
+  cuda_check(cudaMemset(arena_, 0, flag_bytes_), "reset_flags memset");
+  cuda_check(cudaDeviceSynchronize(), "reset_flags sync");
+  host_->ready_words()[rank_].v.store(0);
+  host_->delivered_words()[rank_].v.store(0);
+  host_->barrier();
+  epoch_ = 0;
+  step_seq_ = 0;
+  xfer_seq_ = 0;
+}
+
 DeviceStatus RingContext::read_status(bool clear) {
   DeviceStatus s;
   cuda_check(cudaMemcpy(&s, status_dev_, sizeof(s), cudaMemcpyDeviceToHost), "read status");

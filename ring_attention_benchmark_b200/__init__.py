@@ -11,3 +11,16 @@ kernel.
 __version__ = "0.1.0"
 
 from ._ext import available as extension_available  # noqa: F401
+
+
+def __getattr__(name):
+    # torch-dependent public classes load on first use
+    if name == "RingAttention":
+        from .models.ring_attention import RingAttention
+
+        return RingAttention
+    if name == "RingRuntime":
+        from .parallel.dist import RingRuntime
+
+        return RingRuntime
+    raise AttributeError(name)

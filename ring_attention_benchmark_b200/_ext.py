@@ -20,6 +20,8 @@ def load():
     if _C is not None:
         return _C
     try:
+        import torch  # noqa: F401  (loads libtorch / libc10 the extension links against)
+
         _C = importlib.import_module("ring_attention_benchmark_b200._C")
     except Exception as exc:  # pragma: no cover - exercised when unbuilt
         _ERR = exc

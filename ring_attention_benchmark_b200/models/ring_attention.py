@@ -1,0 +1,113 @@
+"""Public API: ring attention over all ranks of the job, fused on B200.
+
+    from ring_attention_benchmark_b200 import RingAttention
+    attn = RingAttention(seq_per_rank=16384, heads=1, head_dim=64, dtype=torch.float32)
+    out = attn(q, k, v)          # q [S, H, D], k/v [S, Hkv, D] on this rank's GPU
+
+Every rank calls it with its own sequence shard.  The whole ring (all
+world-size key/value blocks, in the reference's order: own block first, then
+the blocks of ranks r-1, r-2, ...) runs in one persistent sm_100a kernel per
+call: the K/V blocks of the other ranks are pulled over NVLink into this
+rank's ring slots inside the kernel while the tensor cores already work on the
+blocks that are present, and the online-softmax state never leaves the chip.
+
+* fp32 inputs are computed with 3xTF32 tensor-core products (fp32-level
+  accuracy); bf16 inputs with bf16 products and fp32 accumulation.
+* ``causal=True`` masks by global token position; ``zigzag=True`` (default for
+  causal) expects the balanced sharding in which rank r holds the global chunks
+  r and 2*world-1-r (see `oracle.zigzag_shard`).
+* GQA: ``heads_kv`` divides ``heads``; only the ``heads_kv`` heads rotate.
+* ``ring_mode="chain"`` forwards each block along the ring (rank r copies block
+  s from rank r-1's slot s-1) instead of reading it from its origin.
+
+The engine allocates its ring slots once (``world`` blocks in the symmetric,
+IPC-mapped arena).  Writing K and V straight into slot 0 (``kv_slot()``) skips
+the per-call copy for bf16 inputs.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .._ext import load
+from ..parallel.dist import RingRuntime
+
+_DTYPES = {torch.float32: "fp32", torch.bfloat16: "bf16"}
+
+
+class RingAttention:
+    def __init__(self, seq_per_rank: int, heads: int = 1, head_dim: int = 64,
+                 heads_kv: Optional[int] = None, dtype: torch.dtype = torch.float32,
+                 causal: bool = False, zigzag: Optional[bool] = None, ring_mode: str = "direct",
+                 runtime: Optional[RingRuntime] = None, timeout_s: float = 10.0):
+        if dtype not in _DTYPES:
+            raise ValueError("dtype must be torch.float32 or torch.bfloat16")
+        if ring_mode not in ("direct", "chain"):
+            raise ValueError("ring_mode must be 'direct' or 'chain'")
+        C = load()
+        self.seq = seq_per_rank
+        self.heads = heads
+        self.heads_kv = heads if heads_kv is None else heads_kv
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.causal = causal
+        self.zigzag = causal if zigzag is None else zigzag
+        prec = _DTYPES[dtype]
+        self._own_runtime = runtime is None
+        if runtime is None:
+            from ..parallel.dist import detect_ranks
+
+            world = detect_ranks().world
+            runtime = RingRuntime(C.FusedRing.arena_bytes(prec, seq_per_rank, self.heads_kv,
+                                                          head_dim, world))
+        self.runtime = runtime
+        self.engine = C.FusedRing(runtime.ctx, prec, seq_per_rank, heads, self.heads_kv, head_dim,
+                                  causal, self.zigzag, ring_mode == "chain", timeout_s)
+
+    @property
+    def rank(self) -> int:
+        return self.runtime.rank
+
+    @property
+    def world(self) -> int:
+        return self.runtime.world
+
+    def _check_inputs(self, q, k, v):
+        exp_q = (self.seq, self.heads, self.head_dim)
+        exp_kv = (self.seq, self.heads_kv, self.head_dim)
+        for name, t, shape in (("q", q, exp_q), ("k", k, exp_kv), ("v", v, exp_kv)):
+            if tuple(t.shape) != shape or t.dtype != self.dtype or not t.is_cuda:
+                raise ValueError(f"{name}: expected CUDA {self.dtype} tensor of shape {shape}, "
+                                 f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                 scale: Optional[float] = None, return_lse: bool = False,
+                 out: Optional[torch.Tensor] = None, check: bool = False):
+        """Attention of this rank's queries over the whole ring; stream-ordered.
+
+        With ``check=True`` the call synchronises and raises if a bounded
+        device-side wait ran out (e.g. a peer rank never arrived).
+        """
+        self._check_inputs(q, k, v)
+        if scale is None:
+            scale = self.head_dim ** -0.5
+        if out is None:
+            out = torch.empty_like(q)
+        lse = (torch.empty(self.seq, self.heads, dtype=torch.float32, device=q.device)
+               if return_lse else None)
+        self.engine.forward(q.contiguous(), k.contiguous(), v.contiguous(), out, lse, float(scale))
+        if check:
+            self.engine.check()
+        return (out, lse) if return_lse else out
+
+    forward = __call__
+
+    def check(self) -> None:
+        self.engine.check()
+
+    def close(self) -> None:
+        self.engine = None
+        if self._own_runtime and self.runtime is not None:
+            self.runtime.close()
+            self.runtime = None

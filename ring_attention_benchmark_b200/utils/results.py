@@ -1,0 +1,115 @@
+"""Output lines of the benchmark programs.
+
+The reference's grammars are kept byte-compatible, label quirks included, so
+existing log parsers keep working:
+
+* comm (``src/loop/ring_loop_*.cu``, RESULT printf at e.g. ``ring_loop_staged.cu``
+  lines 240-244): ``staged_Isendrecv`` prints ``backend=isendrecv`` and both
+  CUDA-aware loops print ``backend=cuda_aware``; GB/s = (np-1)*bytes / avg ms.
+* attention (``src/attention/*_gpu_bench.cu``): a header
+  ``<label> bench: warmup=W iters=I`` and one ``avg_total=… ms …`` line whose
+  fields depend on the backend.
+
+Fields the reference does not print are appended after its own fields
+(``step_ms=``, ``TFLOPs=``, ``roofline_frac=``, ...) and every result can also be
+appended as one JSON record to the file named by ``RAB_RESULTS_JSONL``.
+"""
+from __future__ import annotations
+
+import json
+import os
+import time
+from typing import Dict, Optional
+
+COMM_LABEL = {
+    "staged": "staged",
+    "staged_Isendrecv": "isendrecv",
+    "cuda_aware": "cuda_aware",
+    "cuda_aware_Isendrecv": "cuda_aware",
+    "nccl": "nccl",
+    "b200_fused": "b200_fused",
+}
+
+ATTN_HEADER = {
+    "staged": "staged bench",
+    "staged_Isendrecv": "staged Isendrecv bench",
+    "staged_Isendrecv_overlap": "staged Isendrecv OVERLAP bench",
+    "cuda_aware": "cuda_aware bench",
+    "cuda_aware_Isendrecv": "CUDA-aware Isendrecv bench",
+    "cuda_aware_Isendrecv_overlap": "CUDA-aware Isendrecv OVERLAP bench",
+    "nccl": "nccl bench",
+    "b200_fused": "b200_fused bench",
+}
+
+ATTN_FIELDS = {
+    "staged": ["D2H", "MPI", "H2D"],
+    "staged_Isendrecv": ["D2H", "MPI", "H2D"],
+    "staged_Isendrecv_overlap": ["D2H", "MPI", "H2D"],
+    "cuda_aware": ["MPI"],
+    "cuda_aware_Isendrecv": ["CUDA-aware"],
+    "cuda_aware_Isendrecv_overlap": ["CUDA-aware"],
+    "nccl": ["NCCL"],
+    "b200_fused": ["prep"],
+}
+
+# Isendrecv programs dump only when ATTENTION_DUMP_OUTPUT is set; the others
+# always dump (reference behaviour, e.g. ring_attention_staged_gpu_bench.cu:469-474).
+DUMP_ALWAYS = {"staged", "cuda_aware", "nccl"}
+
+
+def gbps(payload_bytes: float, ms: float) -> Optional[float]:
+    if ms <= 0 or payload_bytes <= 0:
+        return None
+    return payload_bytes / (ms / 1e3) / 1e9
+
+
+def _g(v: Optional[float]) -> str:
+    return "n/a" if v is None else f"{v:.3f}"
+
+
+def comm_result_line(backend: str, nbytes: int, ranks: int, warmup: int, iters: int,
+                     avg: Dict[str, float]) -> str:
+    payload = (ranks - 1) * nbytes
+    total = avg["total"]
+    label = COMM_LABEL[backend]
+    head = f"RESULT backend={label} bytes={nbytes} ranks={ranks} warmup={warmup} iters={iters} "
+    if backend in ("staged", "staged_Isendrecv"):
+        return head + (f"avg_d2h_ms={avg['d2h']:.3f} avg_mpi_ms={avg['mpi']:.3f} "
+                       f"avg_h2d_ms={avg['h2d']:.3f} avg_total_ms={total:.3f} "
+                       f"total_GBps={_g(gbps(payload, total))} mpi_GBps={_g(gbps(payload, avg['mpi']))}")
+    if backend in ("cuda_aware", "cuda_aware_Isendrecv"):
+        return head + (f"avg_mpi_ms={avg['mpi']:.3f} avg_total_ms={total:.3f} "
+                       f"total_GBps={_g(gbps(payload, total))} mpi_GBps={_g(gbps(payload, avg['mpi']))}")
+    if backend == "nccl":
+        return head + (f"avg_nccl_ms={avg['mpi']:.3f} avg_total_ms={total:.3f} "
+                       f"total_GBps={_g(gbps(payload, total))} nccl_GBps={_g(gbps(payload, avg['mpi']))}")
+    # b200_fused: p2p = host-timed launch+sync, kernel = device-timed ring kernel
+    return head + (f"avg_p2p_ms={avg['mpi']:.3f} avg_total_ms={total:.3f} "
+                   f"total_GBps={_g(gbps(payload, total))} p2p_GBps={_g(gbps(payload, avg['mpi']))} "
+                   f"avg_kernel_ms={avg['kernel']:.3f} kernel_GBps={_g(gbps(payload, avg['kernel']))}")
+
+
+def attn_header(backend: str, warmup: int, iters: int) -> str:
+    return f"{ATTN_HEADER[backend]}: warmup={warmup} iters={iters}"
+
+
+def attn_result_line(backend: str, avg: Dict[str, float], extra: Optional[Dict] = None) -> str:
+    parts = [f"avg_total={avg['total']:.3f} ms"]
+    for f in ATTN_FIELDS[backend]:
+        parts.append(f"avg_{f}={avg.get(f, 0.0):.3f}")
+    parts += [f"avg_attn={avg.get('attn', 0.0):.3f}", f"avg_merge={avg.get('merge', 0.0):.3f}",
+              f"avg_final={avg.get('final', 0.0):.3f}"]
+    line = " ".join(parts)
+    if extra:
+        line += " " + " ".join(f"{k}={v}" for k, v in extra.items())
+    return line
+
+
+def append_jsonl(record: Dict) -> None:
+    path = os.environ.get("RAB_RESULTS_JSONL")
+    if not path:
+        return
+    rec = dict(record)
+    rec.setdefault("time", time.time())
+    with open(path, "a") as f:
+        f.write(json.dumps(rec, sort_keys=True) + "\n")
