@@ -194,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_final = bars + 4 * NS + 6;
   uint64_t* drain = bars + 4 * NS + 7;
   __shared__ uint32_t tmem_slot;
+  __shared__ int s_copy_ok;
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -414,22 +415,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.ring_chain) {
           src = reinterpret_cast<const uint4*>(p.peer_slots[left] + (size_t)(s - 1) * p.slot_bytes);
           src_flags = p.flags_peer[left];
-          if (ct == 0) {
-            ok = (s == 1) ? wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st,
-                                      kSitePeerReady, left, tmo)
-                          : wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true,
-                                      st, kSitePeerReady, left, tmo);
-          }
         } else {
           const int origin = ((p.rank - s) % p.world + p.world) % p.world;
           src = reinterpret_cast<const uint4*>(p.peer_slots[origin]);
           src_flags = p.flags_peer[origin];
-          if (ct == 0)
-            ok = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, origin,
-                           tmo);
+        }
+        if (ct == 0) {
+          bool w;
+          if (p.ring_chain && s > 1)
+            w = wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true, st,
+                          kSitePeerReady, s, tmo);
+          else
+            w = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, s, tmo);
+          s_copy_ok = (w && st_read_error(st) == 0) ? 1 : 0;
         }
         named_bar_sync(1, 64);
-        ok = st_read_error(st) == 0;
+        ok = s_copy_ok != 0;  // one decision for all 64 copy threads
         if (!ok) break;
         uint4* dst = reinterpret_cast<uint4*>(p.local_slots + (size_t)s * p.slot_bytes);
         size_t i = beg + ct;
@@ -516,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int cls = classify(p, it, v, kN, tpb, &k_lo, &q_lo);
         if (cls == 0) continue;
         const int b = g & 1;
-        ok = mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo);
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo));
         if (!ok) break;
         tc_fence_after();
         const uint32_t s_tm = tmem + lane_base + (b ? C::kColS1 : C::kColS0);
@@ -544,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // O holds PV of earlier tiles: wait until the last PV landed, then scale rows
-          ok = mbar_wait(pv_done, (g - 1) & 1, st, kSitePvDone, tmo);
+          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (g - 1) & 1, st, kSitePvDone, tmo));
           if (!ok) break;
           tc_fence_after();
           const uint32_t o_tm = tmem + lane_base + C::kColO;
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- epilogue ----
       const bool have = j > 0;
       if (have) {
-        ok = mbar_wait(o_final, final_count & 1, st, kSiteOReady, tmo);
+        ok = __all_sync(0xffffffffu, mbar_wait(o_final, final_count & 1, st, kSiteOReady, tmo));
         ++final_count;
         if (!ok) break;
         tc_fence_after();

@@ -1,0 +1,58 @@
+"""Multi-GPU ring tests: child processes, one rank per GPU, started by the
+local launcher (its watchdog stops every rank as soon as one fails).  Skipped
+when fewer than two GPUs are visible."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WORKER = os.path.join(ROOT, "tests", "_ring_worker.py")
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _ngpus():
+    import torch
+
+    return torch.cuda.device_count()
+
+
+def _run(np, *args, timeout=240):
+    if _ngpus() < np:
+        pytest.skip(f"needs {np} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", RAB_TIMEOUT_S="20")
+    cmd = [sys.executable, "-m", "ring_attention_benchmark_b200.launch", "-np", str(np),
+           "--timeout", str(timeout), sys.executable, WORKER] + [str(a) for a in args]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=timeout + 60)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+    return r.stdout
+
+
+@pytest.mark.parametrize("mode", ["direct", "chain"])
+def test_fused_fp32_two_ranks(mode):
+    _run(2, "fused", "fp32", 0, 1, 1, 64, 1024, mode)
+
+
+def test_fused_bf16_causal_gqa_two_ranks():
+    _run(2, "fused", "bf16", 1, 8, 2, 128, 1024, "direct")
+
+
+def test_comm_backends_two_ranks():
+    out = _run(2, "comm", 1 << 20)
+    assert "comm b200_fused" in out
+
+
+def test_attention_backends_two_ranks():
+    out = _run(2, "attn", 512)
+    assert "attn b200_fused" in out
+
+
+def test_fused_all_gpus():
+    n = _ngpus()
+    if n < 4:
+        pytest.skip("needs 4+ GPUs")
+    _run(n, "fused", "fp32", 0, 1, 1, 64, 2048, "direct")
+    _run(n, "fused", "bf16", 1, 4, 1, 128, 1024, "chain")
