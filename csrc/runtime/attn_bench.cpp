@@ -31,7 +31,7 @@
 #include <chrono>
 #include <cstring>
 #include <memory>
-#include <sstream>
+#include "strfmt.h"
 #include <stdexcept>
 #include <vector>
 
@@ -185,10 +185,10 @@ struct AttnBench::Impl {
   void check_dev(const char* what) {
     const DeviceStatus s = ctx.read_status(true);
     if (s.code != 0) {
-      std::ostringstream os;
-      os << what << ": device wait timed out (site " << s.where << ", block " << s.block << ")";
-      ctx.host().abort(os.str());
-      throw RankFailure(os.str());
+      const std::string msg = strfmt("rank %d: %s: device wait timed out (site %u, block %u)",
+                                     rank, what, s.where, s.block);
+      ctx.host().abort(msg);
+      throw RankFailure(msg);
     }
   }
 
@@ -240,6 +240,8 @@ struct AttnBench::Impl {
                "reset m");
     cuda_check(cudaMemset(l_run, 0, rows * sizeof(float)), "reset l");
     cuda_check(cudaMemset(acc_run, 0, rows * o.dim * sizeof(float)), "reset acc");
+    // peers write into our receive buffer once the next barrier releases them
+    cuda_check(cudaDeviceSynchronize(), "reset sync");
   }
 
   // device-to-device step through the IPC mapping (see comm_bench.cpp)

@@ -23,7 +23,7 @@
 
 #include <chrono>
 #include <cstring>
-#include <sstream>
+#include "strfmt.h"
 #include <stdexcept>
 #include <vector>
 
@@ -127,11 +127,11 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   auto check_dev_status = [&](const char* what) {
     const DeviceStatus s = ctx.read_status(true);
     if (s.code != 0) {
-      std::ostringstream os;
-      os << what << ": device wait timed out (site " << s.where << ", block " << s.block
-         << ", detail " << s.detail << ")";
-      ctx.host().abort(os.str());
-      throw RankFailure(os.str());
+      const std::string msg =
+          strfmt("rank %d: %s: device wait timed out (site %u, block %u, detail %u)", rank, what,
+                 s.where, s.block, s.detail);
+      ctx.host().abort(msg);
+      throw RankFailure(msg);
     }
   };
 
@@ -180,6 +180,7 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   if (o.precheck && np > 1) {
     cuda_check(cudaMemcpy(d1, h_init.data(), o.bytes, cudaMemcpyHostToDevice), "H2D init");
     cuda_check(cudaMemset(d2, 0, o.bytes), "memset");
+    cuda_check(cudaDeviceSynchronize(), "reset sync");  // peers may write d2 after the barrier
     ctx.host().barrier();
     size_t cur = off1, next = off2;
     double a = 0, b = 0, c = 0;
@@ -189,11 +190,9 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
       cuda_check(cudaMemcpy(&first, ctx.local(next), 4, cudaMemcpyDeviceToHost), "D2H check");
       const int src = ((rank - s - 1) % np + np) % np;
       if (first != src * 1000.0f && res.precheck_ok) {
-        std::ostringstream os;
-        os << "rank " << rank << " step " << s << ": received " << first << ", expected "
-           << src * 1000.0f;
         res.precheck_ok = false;
-        res.precheck_msg = os.str();
+        res.precheck_msg = strfmt("rank %d step %d: received %g, expected %g", rank, s,
+                                  static_cast<double>(first), src * 1000.0);
       }
       std::swap(cur, next);
     }
@@ -209,6 +208,7 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   for (int rep = 0; rep < o.warmup + o.iters; ++rep) {
     cuda_check(cudaMemcpy(d1, h_init.data(), o.bytes, cudaMemcpyHostToDevice), "H2D reset");
     cuda_check(cudaMemset(d2, 0, o.bytes), "memset");
+    cuda_check(cudaDeviceSynchronize(), "reset sync");
     double t_d2h = 0, t_mpi = 0, t_h2d = 0, t_kernel = 0;
     ctx.host().barrier();
     const double t0 = wall_ms();

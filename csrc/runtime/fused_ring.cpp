@@ -1,5 +1,5 @@
 // fused_ring.cpp - host side of the `b200_fused` ring attention engine.
-#include <sstream>
+#include "strfmt.h"
 #include <stdexcept>
 
 #include "drivers.h"
@@ -102,11 +102,11 @@ void FusedRing::forward(const void* q, const void* k, const void* v, void* out, 
 void FusedRing::check() {
   const DeviceStatus s = ctx_.read_status(true);
   if (s.code != 0) {
-    std::ostringstream os;
-    os << "rank " << ctx_.rank() << ": fused ring attention wait timed out (site " << s.where
-       << ", block " << s.block << ", detail " << s.detail << ")";
-    ctx_.host().abort(os.str());
-    throw RankFailure(os.str());
+    const std::string msg =
+        strfmt("rank %d: fused ring attention wait timed out (site %u, block %u, detail %u)",
+               ctx_.rank(), s.where, s.block, s.detail);
+    ctx_.host().abort(msg);
+    throw RankFailure(msg);
   }
 }
 

@@ -9,7 +9,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
-#include <sstream>
+#include "strfmt.h"
 #include <thread>
 
 namespace rab {
@@ -114,10 +114,8 @@ std::string HostComm::abort_message() const {
 
 void HostComm::check_abort() const {
   if (aborted()) {
-    std::ostringstream os;
-    os << "rank " << rank_ << ": job aborted by rank " << seg_->abort_rank.load() << ": "
-       << abort_message();
-    throw RankFailure(os.str());
+    throw RankFailure(strfmt("rank %d: job aborted by rank %d: %s", rank_,
+                             seg_->abort_rank.load(), abort_message().c_str()));
   }
 }
 
@@ -130,10 +128,10 @@ void HostComm::abort(const std::string& msg) {
 }
 
 void HostComm::fail_timeout(const std::string& what) {
-  std::ostringstream os;
-  os << "rank " << rank_ << ": timed out after " << timeout_s_ << " s " << what;
-  abort(os.str());
-  throw RankFailure(os.str());
+  const std::string msg = strfmt("rank %d: timed out after %.1f s %s", rank_, timeout_s_,
+                                 what.c_str());
+  abort(msg);
+  throw RankFailure(msg);
 }
 
 void HostComm::barrier() {
@@ -153,11 +151,10 @@ void HostComm::barrier() {
     if ((++spins & 255) == 0) {
       heartbeat();
       if ((now_ns() - t0) * 1e-9 > timeout_s_) {
-        std::ostringstream os;
-        os << "in barrier " << gen << "; missing ranks:";
+        std::string what = strfmt("in barrier %llu; missing ranks:", (unsigned long long)gen);
         for (int r = 0; r < world_; ++r)
-          if (seg_->arrive[r].v.load() < gen) os << ' ' << r;
-        fail_timeout(os.str());
+          if (seg_->arrive[r].v.load() < gen) what += strfmt(" %d", r);
+        fail_timeout(what);
       }
     }
     cpu_relax(spins);
@@ -194,9 +191,8 @@ void HostComm::wait_at_least(const std::atomic<uint64_t>& word, uint64_t value, 
     if ((++spins & 255) == 0) {
       heartbeat();
       if ((now_ns() - t0) * 1e-9 > timeout_s_) {
-        std::ostringstream os;
-        os << "waiting for " << what << " of rank " << peer << " to reach " << value;
-        fail_timeout(os.str());
+        fail_timeout(strfmt("waiting for %s of rank %d to reach %llu", what, peer,
+                            (unsigned long long)value));
       }
     }
     cpu_relax(spins);
@@ -256,10 +252,8 @@ void HostComm::ring_sendrecv(const void* send, void* recv, size_t bytes) {
     if ((++spins & 255) == 0) {
       heartbeat();
       if ((now_ns() - t_last) * 1e-9 > timeout_s_) {
-        std::ostringstream os;
-        os << "in ring_sendrecv (sent " << sent << "/" << nfrag << " fragments to rank " << right
-           << ", received " << got << "/" << nfrag << " from rank " << left << ")";
-        fail_timeout(os.str());
+        fail_timeout(strfmt("in ring_sendrecv (sent %zu/%zu fragments to rank %d, received "
+                            "%zu/%zu from rank %d)", sent, nfrag, right, got, nfrag, left));
       }
     }
     cpu_relax(spins);

@@ -2,24 +2,20 @@
 #include "ring_context.h"
 
 #include <cstring>
-#include <sstream>
+#include "strfmt.h"
 #include <stdexcept>
 
 namespace rab {
 
 void cuda_check(cudaError_t err, const char* what) {
   if (err != cudaSuccess) {
-    std::ostringstream os;
-    os << what << ": " << cudaGetErrorString(err);
-    throw std::runtime_error(os.str());
+    throw std::runtime_error(strfmt("%s: %s", what, cudaGetErrorString(err)));
   }
 }
 
 void nccl_check(ncclResult_t res, const char* what) {
   if (res != ncclSuccess) {
-    std::ostringstream os;
-    os << what << ": " << ncclGetErrorString(res);
-    throw std::runtime_error(os.str());
+    throw std::runtime_error(strfmt("%s: %s", what, ncclGetErrorString(res)));
   }
 }
 
@@ -57,10 +53,8 @@ RingContext::~RingContext() {
 size_t RingContext::arena_alloc(size_t bytes, size_t align) {
   size_t off = (arena_used_ + align - 1) / align * align;
   if (off + bytes > arena_bytes_) {
-    std::ostringstream os;
-    os << "arena_alloc: out of arena space (need " << off + bytes << " of " << arena_bytes_
-       << " bytes)";
-    throw std::runtime_error(os.str());
+    throw std::runtime_error(strfmt("arena_alloc: out of arena space (need %zu of %zu bytes)",
+                                    off + bytes, arena_bytes_));
   }
   arena_used_ = off + bytes;
   return off;

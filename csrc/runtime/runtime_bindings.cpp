@@ -31,9 +31,13 @@ void check_cpu_contig(const torch::Tensor& t, const char* name) {
 
 }  // namespace
 
+namespace rab {
+void install_crash_handler();
+}
+
 void register_runtime(py::module_& m) {
-  static py::exception<RankFailure> rank_failure(m, "RankFailure", PyExc_RuntimeError);
-  (void)rank_failure;
+  rab::install_crash_handler();
+  py::register_exception<RankFailure>(m, "RankFailure", PyExc_RuntimeError);
 
   py::class_<HostComm>(m, "HostComm")
       .def(py::init<const std::string&, int, int, bool, size_t, double>(), py::arg("name"),

@@ -5,7 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
-#include <sstream>
+#include "strfmt.h"
 #include <stdexcept>
 
 namespace rab {
@@ -33,15 +33,14 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 std::string tmap_describe(int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                           const uint32_t* box) {
-  std::ostringstream os;
-  os << "rank=" << rank << " dims=[";
-  for (int i = 0; i < rank; ++i) os << (i ? "," : "") << dims[i];
-  os << "] strides=[";
-  for (int i = 0; i + 1 < rank; ++i) os << (i ? "," : "") << strides_bytes[i];
-  os << "] box=[";
-  for (int i = 0; i < rank; ++i) os << (i ? "," : "") << box[i];
-  os << "]";
-  return os.str();
+  std::string s = strfmt("rank=%d dims=[", rank);
+  for (int i = 0; i < rank; ++i) s += strfmt(i ? ",%llu" : "%llu", (unsigned long long)dims[i]);
+  s += "] strides=[";
+  for (int i = 0; i + 1 < rank; ++i)
+    s += strfmt(i ? ",%llu" : "%llu", (unsigned long long)strides_bytes[i]);
+  s += "] box=[";
+  for (int i = 0; i < rank; ++i) s += strfmt(i ? ",%u" : "%u", box[i]);
+  return s + "]";
 }
 
 CUtensorMap make_tmap(const void* base, TmapDtype dtype, int rank, const uint64_t* dims,
@@ -79,10 +78,9 @@ CUtensorMap make_tmap(const void* base, TmapDtype dtype, int rank, const uint64_
       CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (res != CUDA_SUCCESS) {
-    std::ostringstream os;
-    os << "cuTensorMapEncodeTiled failed (" << static_cast<int>(res)
-       << "): " << tmap_describe(rank, dims, strides_bytes, box);
-    throw std::runtime_error(os.str());
+    throw std::runtime_error(strfmt("cuTensorMapEncodeTiled failed (%d): %s",
+                                    static_cast<int>(res),
+                                    tmap_describe(rank, dims, strides_bytes, box).c_str()));
   }
   return map;
 }
