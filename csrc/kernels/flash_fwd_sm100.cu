@@ -781,10 +781,13 @@ template <Prec P, int D>
 int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
                 cudaStream_t stream) {
   using C = Cfg<P, D>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // the shared-memory opt-in is a per-device function attribute
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
     set_smem_attr<P, D>();
-    attr_done = true;
+    if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
   if (p.Skv % C::kN != 0)
     throw std::runtime_error("flash: keys per block must be a multiple of " +
