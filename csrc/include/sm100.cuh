@@ -108,9 +108,9 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tensor) loads.  No .multicast::cluster form is provided on purpose:
-// tiles may come from peer-mapped memory and a multicast load of another GPU's
-// memory is not allowed in this code base.
+// TMA (tensor) loads, plain form only.  No cluster-broadcast variant exists in
+// this code base: ring slots can be peer-mapped memory of another GPU, and a
+// broadcast load whose source is another GPU's memory must never be issued.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
