@@ -119,7 +119,7 @@ def main() -> int:
     # ---- device-timed steps ----
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    sampler = ClockSampler(gpus=[rt.device] if world == 1 else None)
+    sampler = ClockSampler(gpus=list(range(world)) if world > 1 else [rt.device])
     torch.cuda.synchronize(dev)
     rt.barrier()
     if rank == 0:
@@ -145,43 +145,66 @@ def main() -> int:
     value = flops_total / (ms_per_step * 1e-3) / 1e12
 
     # ---- end to end through the public call: H2D inputs, D2H output ----
+    # Every step copies its Q/K/V from pinned host memory and reads its output
+    # back.  The copies of step i+1 overlap the attention of step i (a copy
+    # stream with double-buffered device inputs), the way a serving loop runs;
+    # the K-step loop is timed as a whole and divided by K.
     e2e = None
     if not args.no_e2e:
         q_h = x.q.to(dtype).pin_memory()
         k_h = x.k.to(dtype).pin_memory()
         v_h = x.v.to(dtype).pin_memory()
-        out_h = torch.empty(q.shape, dtype=dtype).pin_memory()
-        qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        for i in range(args.warmup + args.steps):
-            flush.fill_(i & 0xFF)
+        outs_h = [torch.empty(q.shape, dtype=dtype).pin_memory() for _ in range(2)]
+        ins = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)) for _ in range(2)]
+        outs_d = [torch.empty_like(q) for _ in range(2)]
+        cstream = torch.cuda.Stream(dev)
+
+        def run_e2e(nsteps):
+            ev_in = [torch.cuda.Event() for _ in range(nsteps)]
+            ev_comp = [torch.cuda.Event() for _ in range(nsteps)]
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            cstream.wait_event(t0)
+
+            def h2d(i):
+                with torch.cuda.stream(cstream):
+                    if i >= 2:
+                        cstream.wait_event(ev_comp[i - 2])  # buffer i%2 is free again
+                    bq, bk, bv = ins[i % 2]
+                    bq.copy_(q_h, non_blocking=True)
+                    bk.copy_(k_h, non_blocking=True)
+                    bv.copy_(v_h, non_blocking=True)
+                    ev_in[i].record(cstream)
+
+            h2d(0)
+            for i in range(nsteps):
+                if i + 1 < nsteps:
+                    h2d(i + 1)
+                stream.wait_event(ev_in[i])
+                bq, bk, bv = ins[i % 2]
+                attn(bq, bk, bv, out=outs_d[i % 2])
+                ev_comp[i].record(stream)
+                with torch.cuda.stream(cstream):
+                    cstream.wait_event(ev_comp[i])
+                    outs_h[i % 2].copy_(outs_d[i % 2], non_blocking=True)
+            stream.wait_stream(cstream)
+            t1.record(stream)
             torch.cuda.synchronize(dev)
-            rt.barrier()
-            j = i - args.warmup
-            if j >= 0:
-                e_s[j].record(stream)
-            qd.copy_(q_h, non_blocking=True)
-            kd.copy_(k_h, non_blocking=True)
-            vd.copy_(v_h, non_blocking=True)
-            o = attn(qd, kd, vd)
-            out_h.copy_(o, non_blocking=True)
-            if j >= 0:
-                e_e[j].record(stream)
-        torch.cuda.synchronize(dev)
+            return t0.elapsed_time(t1)
+
+        run_e2e(args.warmup)
+        rt.barrier()
+        e2e_ms = rt.reduce_max([run_e2e(args.steps)])[0] / args.steps
         attn.check()
-        loc = [s.elapsed_time(e) for s, e in zip(e_s, e_e)]
-        mx = []
-        for c in range(0, len(loc), 16):
-            mx += rt.reduce_max(loc[c:c + 16])
-        e2e_ms = statistics.mean(mx)
-        ok = bool(torch.isfinite(out_h).all())
+        ok = bool(torch.isfinite(outs_h[0]).all()) and bool(
+            torch.allclose(outs_h[(args.steps - 1) % 2], out.cpu()))
         e2e = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": int((q_h.numel() + k_h.numel() + v_h.numel())
                                          * q_h.element_size()),
-               "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()),
-               "output_finite": ok}
+               "d2h_bytes_per_step": int(outs_h[0].numel() * outs_h[0].element_size()),
+               "output_matches_device_timed_run": ok,
+               "schedule": "copies of step i+1 overlap step i; K-step loop timed as a whole"}
 
     nsplit = attn.engine.nsplit
     per_step = (2 if args.dtype == "fp32" else 0) + 1 + (1 if nsplit > 1 else 0)
