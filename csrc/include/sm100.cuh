@@ -350,6 +350,16 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& big, uint32_t& sma
   small = f32_to_tf32(x - __uint_as_float(big));
 }
 
+// Same split with integer ALU ops only (no conversion-pipe instruction): big is
+// x rounded to tf32 by adding half a tf32 ulp to the bit pattern and clearing
+// the low 13 bits; small = x - big is exact in fp32 (Sterbenz) and is read by
+// the tensor core as tf32, dropping its low bits, so the represented value is
+// within 2^-21 |x| of x.  For finite |x| < 2^127.
+__device__ __forceinline__ void split_tf32_alu(float x, uint32_t& big, uint32_t& small) {
+  big = (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
+  small = __float_as_uint(x - __uint_as_float(big));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

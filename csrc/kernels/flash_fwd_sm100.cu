@@ -480,10 +480,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const float4 x = __ldg(qp + c / 4 + i);
-              split_tf32(x.x, big[4 * i + 0], small[4 * i + 0]);
-              split_tf32(x.y, big[4 * i + 1], small[4 * i + 1]);
-              split_tf32(x.z, big[4 * i + 2], small[4 * i + 2]);
-              split_tf32(x.w, big[4 * i + 3], small[4 * i + 3]);
+              split_tf32_alu(x.x, big[4 * i + 0], small[4 * i + 0]);
+              split_tf32_alu(x.y, big[4 * i + 1], small[4 * i + 1]);
+              split_tf32_alu(x.z, big[4 * i + 2], small[4 * i + 2]);
+              split_tf32_alu(x.w, big[4 * i + 3], small[4 * i + 3]);
             }
             tmem_st32(tmem + lane_base + C::kColQ + c, big);
             tmem_st32(tmem + lane_base + C::kColQ + C::kQCols + c, small);
@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const float e = ex2_approx(fmaf(__uint_as_float(sr[c + i]), sl2, -m_use));
               rowsum += e;
-              split_tf32(e, pb[i], ps[i]);
+              split_tf32_alu(e, pb[i], ps[i]);
             }
             tmem_st32(s_tm + c, pb);
             tmem_st32(tmem + lane_base + (b ? C::kColPs1 : C::kColPs0) + c, ps);
