@@ -1,0 +1,67 @@
+#!/bin/bash
+# benchmark_attention.sh - ring attention benchmark over backends and sizes.
+#
+# Env / benchmark.env keys: NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS LAUNCHER
+# (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
+# SRUN_MPI_TYPE SRUN_EXTRA_ARGS, plus RAB_DATA (normal | ref_compat), RAB_PREC (fp32 |
+# bf16), RAB_KERNEL (tcgen05 | simt), RAB_RING_MODE (direct | chain).  SIZES
+# overrides ATTENTION_SIZES.  Stops at the first
+# failing backend/size, like the reference wrapper.
+set -euo pipefail
+
+SCRIPT_DIR="$(cd "$(dirname "$0")" && pwd)"
+cd "${SCRIPT_DIR}"
+# shellcheck disable=SC1091
+source "${SCRIPT_DIR}/ring_env.sh"
+
+CONFIG=${CONFIG:-benchmark.env}
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS \
+  LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS \
+  RAB_DATA RAB_PREC RAB_KERNEL RAB_RING_MODE
+configure_runtime_env
+
+if under_launcher; then
+  echo "ERROR: benchmark_attention.sh should be run from a normal shell; it launches the ranks itself." >&2
+  exit 1
+fi
+
+NP=${NP:-2}
+WARMUP=${WARMUP:-10}
+ITERS=${ITERS:-100}
+export RAB_DATA RAB_PREC RAB_KERNEL RAB_RING_MODE 2>/dev/null || true
+ATTENTION_SIZES=${ATTENTION_SIZES:-"262144 524288 1048576"}
+SIZES=${SIZES:-${ATTENTION_SIZES}}
+ATTENTION_BACKENDS=${ATTENTION_BACKENDS:-"staged staged_Isendrecv staged_Isendrecv_overlap cuda_aware cuda_aware_Isendrecv cuda_aware_Isendrecv_overlap nccl b200_fused"}
+LAUNCHER=${LAUNCHER:-local}
+export LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
+
+BIN_DIR="${SCRIPT_DIR}/bin"
+
+echo "========== Ring Attention Benchmark =========="
+echo "Date: $(date)"
+echo "Hostname: $(hostname)"
+echo "launcher=${LAUNCHER} np=${NP} warmup=${WARMUP} iters=${ITERS}"
+echo "sizes=${SIZES}"
+echo "attention_backends=${ATTENTION_BACKENDS}"
+echo ""
+
+for backend in ${ATTENTION_BACKENDS}; do
+  exe="${BIN_DIR}/ring_attention_${backend}_gpu_bench"
+  if [[ ! -f "${exe}" ]]; then
+    echo "SKIP backend=${backend} (unknown backend)"
+    echo ""
+    continue
+  fi
+  echo "===== backend=${backend} ====="
+  for size in ${SIZES}; do
+    echo "--- kv_size=${size} bytes ---"
+    if ! launch_ranks "${NP}" "${exe}" "${size}" "${WARMUP}" "${ITERS}"; then
+      echo "ERROR: ${backend} failed with kv_size=${size}"
+      exit 1
+    fi
+  done
+  echo ""
+done
+
+echo "========== Done =========="
+echo "Finished at: $(date)"

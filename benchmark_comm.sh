@@ -1,0 +1,63 @@
+#!/bin/bash
+# benchmark_comm.sh - comm-only ring benchmark over backends and sizes.
+#
+# Env / benchmark.env keys: NP WARMUP ITERS SIZES COMM_SIZES BACKENDS LAUNCHER
+# (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
+# SRUN_MPI_TYPE SRUN_EXTRA_ARGS.  SIZES overrides COMM_SIZES.  Stops at the first
+# failing backend/size, like the reference wrapper.
+set -euo pipefail
+
+SCRIPT_DIR="$(cd "$(dirname "$0")" && pwd)"
+cd "${SCRIPT_DIR}"
+# shellcheck disable=SC1091
+source "${SCRIPT_DIR}/ring_env.sh"
+
+CONFIG=${CONFIG:-benchmark.env}
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS \
+  LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
+configure_runtime_env
+
+if under_launcher; then
+  echo "ERROR: benchmark_comm.sh should be run from a normal shell; it launches the ranks itself." >&2
+  exit 1
+fi
+
+NP=${NP:-2}
+WARMUP=${WARMUP:-10}
+ITERS=${ITERS:-100}
+COMM_SIZES=${COMM_SIZES:-"262144 524288 1048576 4194304 16777216"}
+SIZES=${SIZES:-${COMM_SIZES}}
+BACKENDS=${BACKENDS:-"staged staged_Isendrecv cuda_aware cuda_aware_Isendrecv nccl b200_fused"}
+LAUNCHER=${LAUNCHER:-local}
+export LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
+
+BIN_DIR="${SCRIPT_DIR}/bin"
+
+echo "========== Communication (Loop) Benchmark =========="
+echo "Date: $(date)"
+echo "Hostname: $(hostname)"
+echo "launcher=${LAUNCHER} np=${NP} warmup=${WARMUP} iters=${ITERS}"
+echo "sizes=${SIZES}"
+echo "backends=${BACKENDS}"
+echo ""
+
+for backend in ${BACKENDS}; do
+  exe="${BIN_DIR}/ring_loop_${backend}"
+  if [[ ! -f "${exe}" ]]; then
+    echo "SKIP backend=${backend} (unknown backend)"
+    echo ""
+    continue
+  fi
+  echo "===== backend=${backend} ====="
+  for size in ${SIZES}; do
+    echo "--- kv_size=${size} bytes ---"
+    if ! launch_ranks "${NP}" "${exe}" "${size}" "${WARMUP}" "${ITERS}"; then
+      echo "ERROR: ${backend} failed with kv_size=${size}"
+      exit 1
+    fi
+  done
+  echo ""
+done
+
+echo "========== Done =========="
+echo "Finished at: $(date)"

@@ -1,0 +1,133 @@
+"""Interface compatibility with the reference benchmark, on CPU: output-line
+grammar (label quirks included), config precedence (environment over file,
+SIZES over the per-family lists), the correctness checker's PASS rule and its
+oracle mode, and the shell scripts."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from ring_attention_benchmark_b200.utils import checker, config, results
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_comm_result_lines_match_reference_grammar():
+    avg = {"d2h": 0.027, "mpi": 0.080, "h2d": 0.028, "total": 0.135, "kernel": 0.0}
+    line = results.comm_result_line("staged", 262144, 2, 10, 100, avg)
+    assert line == ("RESULT backend=staged bytes=262144 ranks=2 warmup=10 iters=100 "
+                    "avg_d2h_ms=0.027 avg_mpi_ms=0.080 avg_h2d_ms=0.028 avg_total_ms=0.135 "
+                    "total_GBps=1.942 mpi_GBps=3.277")
+    assert results.comm_result_line("staged_Isendrecv", 4, 2, 1, 1, avg).startswith(
+        "RESULT backend=isendrecv ")
+    ca = results.comm_result_line("cuda_aware_Isendrecv", 4, 2, 1, 1, avg)
+    assert ca.startswith("RESULT backend=cuda_aware ") and "avg_mpi_ms=" in ca
+    nc = results.comm_result_line("nccl", 4, 2, 1, 1, avg)
+    assert re.search(r"avg_nccl_ms=\S+ avg_total_ms=\S+ total_GBps=\S+ nccl_GBps=\S+$", nc)
+    one = results.comm_result_line("nccl", 4, 1, 1, 1, avg)
+    assert "total_GBps=n/a" in one  # one rank: nothing moves
+
+
+def test_attention_lines():
+    avg = {"total": 24.677, "D2H": 0.027, "MPI": 0.080, "H2D": 0.028, "attn": 24.218,
+           "merge": 0.079, "final": 0.269}
+    assert results.attn_header("staged", 10, 100) == "staged bench: warmup=10 iters=100"
+    assert results.attn_result_line("staged", avg) == (
+        "avg_total=24.677 ms avg_D2H=0.027 avg_MPI=0.080 avg_H2D=0.028 avg_attn=24.218 "
+        "avg_merge=0.079 avg_final=0.269")
+    assert results.attn_header("cuda_aware_Isendrecv_overlap", 1, 2) == \
+        "CUDA-aware Isendrecv OVERLAP bench: warmup=1 iters=2"
+    assert "avg_CUDA-aware=" in results.attn_result_line("cuda_aware_Isendrecv", avg)
+    assert "avg_NCCL=" in results.attn_result_line("nccl", avg)
+
+
+def test_config_precedence(tmp_path):
+    f = tmp_path / "benchmark.env"
+    f.write_text('# comment\nNP_LIST="2 4"\nexport WARMUP=3\nCOMM_SIZES="1024 2048"\n'
+                 "ATTENTION_SIZES=256\n")
+    cfg = config.load_config(str(f), env={"WARMUP": "7"})
+    assert cfg["NP_LIST"] == "2 4" and cfg["WARMUP"] == "7"
+    assert config.sizes_for("comm", cfg) == [1024, 2048]
+    assert config.sizes_for("attention", cfg) == [256]
+    cfg2 = config.load_config(str(f), env={"SIZES": "4096"})
+    assert config.sizes_for("comm", cfg2) == [4096]
+
+
+def test_checker_rule(tmp_path):
+    a = np.linspace(1e4, 7e4, 64, dtype=np.float32)
+    b = a * (1 + 5e-6)  # above ABS_TOL but within REL_TOL -> PASS (the reference's OR rule)
+    r = checker.compare_arrays([a], [b.astype(np.float32)], 1e-3, 1e-5)
+    assert r.passed and r.max_abs > 1e-3
+    c = a.copy()
+    c[3] += 1.0
+    r2 = checker.compare_arrays([a], [c], 1e-3, 1e-5)
+    assert not r2.passed
+    assert r2.line("x").startswith("x: FAIL elements=64 max_abs_err=")
+
+
+def test_checker_oracle_mode(tmp_path):
+    outs = checker.oracle_outputs(2, 256 * 64 * 4 // 64 * 1)  # 64 tokens per rank
+    for r, o in enumerate(outs):
+        o.astype("<f4").tofile(tmp_path / f"ring_output_rank{r}.bin")
+    assert checker.check_oracle(str(tmp_path), 2, 256 * 64 * 4 // 64).passed
+    bad = outs[1].copy()
+    bad[0] += 0.1
+    bad.astype("<f4").tofile(tmp_path / "ring_output_rank1.bin")
+    assert not checker.check_oracle(str(tmp_path), 2, 256 * 64 * 4 // 64).passed
+
+
+@pytest.mark.parametrize("script", ["benchmark_comm.sh", "benchmark_attention.sh", "run_suite.sh",
+                                    "check_attention_correctness.sh", "collect_env.sh",
+                                    "ring_env.sh", "launch_local.example.sh",
+                                    "launch_mpirun.example.sh", "batch_slurm.example.sh"])
+def test_scripts_parse(script):
+    r = subprocess.run(["bash", "-n", os.path.join(ROOT, script)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+def test_env_overrides_config_in_shell(tmp_path):
+    f = tmp_path / "c.env"
+    f.write_text('NP=4\nWARMUP=9\n')
+    cmd = (f"source {ROOT}/ring_env.sh; NP=2; "
+           f"source_config_preserving_env {f} NP WARMUP; echo $NP $WARMUP")
+    r = subprocess.run(["bash", "-c", cmd], capture_output=True, text=True)
+    assert r.stdout.split() == ["2", "9"]
+
+
+def test_wrappers_refuse_inside_a_launched_rank():
+    env = dict(os.environ, OMPI_COMM_WORLD_RANK="0")
+    r = subprocess.run([os.path.join(ROOT, "benchmark_comm.sh")], env=env, capture_output=True,
+                       text=True, cwd=ROOT)
+    assert r.returncode == 1 and "normal shell" in r.stderr
+
+
+def test_run_suite_prepares_run_dir(tmp_path):
+    env = dict(os.environ, BUILD="0", COLLECT_ENV="0", RESULTS_ROOT=str(tmp_path), RUN_LABEL="t",
+               NP_LIST="1 2")
+    r = subprocess.run([os.path.join(ROOT, "run_suite.sh")], env=env, capture_output=True,
+                       text=True, cwd=ROOT)
+    assert r.returncode == 0, r.stderr
+    for name in ("manifest.txt", "run_context.env", "launch_examples.txt"):
+        assert (tmp_path / "t" / name).is_file()
+    ex = (tmp_path / "t" / "launch_examples.txt").read_text()
+    assert 'NP="2"' in ex and "benchmark_attention.sh" in ex and 'LAUNCHER="torchrun"' in ex
+
+
+def test_bin_programs_exist_for_every_backend():
+    for b in ("staged", "staged_Isendrecv", "cuda_aware", "cuda_aware_Isendrecv", "nccl",
+              "b200_fused"):
+        assert os.access(os.path.join(ROOT, "bin", f"ring_loop_{b}"), os.X_OK)
+    for b in ("staged", "staged_Isendrecv", "staged_Isendrecv_overlap", "cuda_aware",
+              "cuda_aware_Isendrecv", "cuda_aware_Isendrecv_overlap", "nccl", "b200_fused"):
+        assert os.access(os.path.join(ROOT, "bin", f"ring_attention_{b}_gpu_bench"), os.X_OK)
+
+
+def test_cli_argument_validation():
+    from ring_attention_benchmark_b200 import cli
+
+    assert cli.comm_main("nccl", []) == 1          # missing size (reference: usage, exit 1)
+    assert cli.comm_main("nccl", ["6"]) == 1       # not a multiple of 4
+    assert cli.attention_main("nccl", ["300"]) == 1  # not a multiple of 256
+    assert cli.comm_main("nope", ["4"]) == 1
