@@ -93,15 +93,120 @@ __global__ void __launch_bounds__(512) p2p_ring_kernel(const RingCopyParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk variant: one elected thread per CTA streams its slice through a
+// 4-stage shared-memory ring with the TMA bulk engine: bulk load of a chunk of
+// the local buffer into shared memory (completion on an mbarrier), then a bulk
+// store of that chunk into the right neighbour's buffer.  Only stores touch
+// peer memory; loads read this GPU's own buffer.
+// ---------------------------------------------------------------------------
+constexpr int kBulkStages = 4;
+constexpr uint32_t kBulkChunk = 32768;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* st,
+                                         uint64_t timeout_ns) {
+  const uint64_t t0 = now_ns();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (st_read_error(st) != 0) return false;
+    if (now_ns() - t0 > timeout_ns) {
+      st_record_timeout(st, kSiteCopySlice, 0);
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32) p2p_ring_bulk_kernel(const RingCopyParams p) {
+  extern __shared__ __align__(128) uint8_t stage_buf[];
+  __shared__ __align__(8) uint64_t bars[kBulkStages];
+  if (threadIdx.x != 0) return;
+  const int c = blockIdx.x;
+  const size_t per = ((p.bytes / gridDim.x) + 15) / 16 * 16;
+  const size_t beg = per * c;
+  const size_t end = beg + per < p.bytes ? beg + per : p.bytes;
+  for (int i = 0; i < kBulkStages; ++i)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bars[i])) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  uint32_t uses[kBulkStages] = {0, 0, 0, 0};
+  for (int s = 0; s < p.nsteps; ++s) {
+    const uint64_t seq = p.base + s;
+    const int sg = p.first_step + s;
+    if (sg > 0 && !wait_ge(p.arrived_local + c, seq, p.status, (uint32_t)s, p.timeout_ns)) return;
+    if (!wait_ge(p.sent_right + c, seq, p.status, 0x10000u | (uint32_t)s, p.timeout_ns)) return;
+    // data this rank received last step (written by the peer's bulk stores) is
+    // read below by the bulk engine: order it after the flag acquire
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    const uint8_t* src = p.buf[sg & 1];
+    uint8_t* dst = p.right_buf[(sg + 1) & 1];
+    int k = 0;
+    for (size_t off = beg; off < end; off += kBulkChunk, ++k) {
+      const int st = k % kBulkStages;
+      const uint32_t n = static_cast<uint32_t>(end - off < kBulkChunk ? end - off : kBulkChunk);
+      uint8_t* sb = stage_buf + st * kBulkChunk;
+      // the stage's previous bulk store must have finished reading shared memory
+      asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kBulkStages - 1) : "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                       smem_addr(&bars[st])),
+                   "r"(n)
+                   : "memory");
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+              "r"(smem_addr(sb)),
+          "l"(src + off), "r"(n), "r"(smem_addr(&bars[st]))
+          : "memory");
+      if (!bar_wait(&bars[st], uses[st] & 1, p.status, p.timeout_ns)) {
+        // unwind: let this CTA's bulk stores finish and give the pending bulk
+        // load a bounded chance to land before shared memory is released
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        bar_wait(&bars[st], uses[st] & 1, nullptr, 100000000ull);
+        return;
+      }
+      ++uses[st];
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + off),
+                   "r"(smem_addr(sb)), "r"(n)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence_system();
+    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.arrived_right + c) : "memory");
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.sent_local + c), "l"(seq + 1)
+                 : "memory");
+  }
+}
+
 }  // namespace
 
 int p2p_ring_launch(const RingCopyParams& p, int slices, cudaStream_t stream) {
   if (p.bytes % 16 != 0) throw std::runtime_error("p2p ring: bytes must be a multiple of 16");
   if (p.nsteps <= 0) return 0;
-  void* args[] = {const_cast<RingCopyParams*>(&p)};
-  // cooperative launch: every slice's CTA must be resident at once
-  return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(p2p_ring_kernel),
-                                                      dim3(slices), dim3(512), args, 0, stream));
+  // Slice c only waits on slice c of the neighbours, so the CTAs need not be
+  // co-resident: a regular launch cannot deadlock.
+  if (p.mode == 1) {
+    const int smem = kBulkStages * kBulkChunk;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(p2p_ring_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem);
+      attr = true;
+    }
+    p2p_ring_bulk_kernel<<<slices, 32, smem, stream>>>(p);
+  } else {
+    p2p_ring_kernel<<<slices, 512, 0, stream>>>(p);
+  }
+  return static_cast<int>(cudaGetLastError());
 }
 
 }  // namespace rab

@@ -123,6 +123,7 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
     rp.bytes = o.bytes;
     rp.status = ctx.status_dev();
     rp.timeout_ns = static_cast<uint64_t>(ctx.host().timeout_s() * 1e9);
+    rp.mode = o.p2p_mode;
   }
   auto check_dev_status = [&](const char* what) {
     const DeviceStatus s = ctx.read_status(true);

@@ -108,7 +108,7 @@ void register_runtime(py::module_& m) {
   m.def(
       "run_comm_bench",
       [](RingContext& ctx, const std::string& backend, size_t bytes, int warmup, int iters,
-         int slices, bool precheck) {
+         int slices, bool precheck, int p2p_mode) {
         CommOptions o;
         o.backend = backend;
         o.bytes = bytes;
@@ -116,6 +116,7 @@ void register_runtime(py::module_& m) {
         o.iters = iters;
         o.slices = slices;
         o.precheck = precheck;
+        o.p2p_mode = p2p_mode;
         CommResult r;
         {
           py::gil_scoped_release nogil;
@@ -124,7 +125,8 @@ void register_runtime(py::module_& m) {
         return r.avg_ms;
       },
       py::arg("ctx"), py::arg("backend"), py::arg("bytes"), py::arg("warmup") = 10,
-      py::arg("iters") = 100, py::arg("slices") = 0, py::arg("precheck") = true);
+      py::arg("iters") = 100, py::arg("slices") = 0, py::arg("precheck") = true,
+      py::arg("p2p_mode") = 0);
   m.def("comm_arena_bytes", &comm_arena_bytes);
 
   py::class_<AttnBench>(m, "AttnBench")
