@@ -127,6 +127,17 @@ void split_tf32(torch::Tensor in, torch::Tensor big, torch::Tensor small) {
                "split_tf32");
 }
 
+void wait_selftest(torch::Tensor flag, int64_t target, double timeout_s, torch::Tensor status) {
+  check_cuda(flag, "flag");
+  TORCH_CHECK(flag.scalar_type() == torch::kInt64 && flag.numel() >= 1, "flag must be int64");
+  const c10::cuda::CUDAGuard guard(flag.device());
+  check_launch(wait_selftest_launch(reinterpret_cast<const uint64_t*>(flag.data_ptr()),
+                                    static_cast<uint64_t>(target),
+                                    static_cast<uint64_t>(timeout_s * 1e9), status_ptr(status),
+                                    cur_stream()),
+               "wait_selftest");
+}
+
 }  // namespace
 }  // namespace rab
 
@@ -148,6 +159,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("m"), py::arg("l"), py::arg("out"), py::arg("lse") = c10::nullopt);
   m.def("cast", &rab::cast, "fp32 <-> bf16 cast");
   m.def("split_tf32", &rab::split_tf32, "fp32 -> tf32 big/small planes");
+  m.def("wait_selftest", &rab::wait_selftest,
+        "bounded device wait on a flag word; records a timeout in the status word");
   register_flash(m);
   register_runtime(m);
 }

@@ -29,6 +29,9 @@ int normalize_launch(const float* acc, const float* m, const float* l, void* out
 
 int cast_f32_bf16_launch(const float* in, void* out, size_t n, cudaStream_t stream);
 int cast_bf16_f32_launch(const void* in, float* out, size_t n, cudaStream_t stream);
+int wait_selftest_launch(const uint64_t* flag, uint64_t target, uint64_t timeout_ns,
+                         DeviceStatus* st, cudaStream_t stream);
+
 int split_tf32_launch(const float* in, float* big, float* small, size_t n, cudaStream_t stream);
 
 }  // namespace rab
