@@ -21,6 +21,12 @@ number runs the same steps through the public `RingAttention` call with the
 inputs copied host->device from pinned memory and the output read back every
 step.  nvidia-smi samples the clocks during the timed loop.
 
+--preset selects the workload: ref-fp32 (the headline above), mha-bf16-causal
+(32 heads, d=128, 16384 tokens per rank, bf16, causal with zigzag sharding) or
+gqa-bf16-long (32 query / 8 key-value heads, d=128, 65536 tokens per rank,
+bf16 N(0,1)*0.5 from seed 1234, causal zigzag); causal FLOPs count the visible
+(query, key) pairs only.
+
 With --gpus N > 1 the script expects torchrun (RANK/WORLD_SIZE/LOCAL_RANK); run
 directly it re-launches itself on N local ranks.
 """
@@ -36,10 +42,16 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-SEQ_PER_RANK = 16384
-HEADS = 1
-HEAD_DIM = 64
 METRIC = "ring_attention_fwd_tflops"
+# name: (tokens per rank, q heads, kv heads, head dim, dtype, causal, input scale, seed)
+PRESETS = {
+    # the reference's full ring attention at its largest ATTENTION_SIZES entry (headline)
+    "ref-fp32": (16384, 1, 1, 64, "fp32", False, 1.0, None),
+    # multi-head bf16, causal with zigzag sharding
+    "mha-bf16-causal": (16384, 32, 32, 128, "bf16", True, 1.0, None),
+    # long-context GQA layer shape: 32 q / 8 kv heads, causal zigzag, N(0,1)*0.5 seed 1234
+    "gqa-bf16-long": (65536, 32, 8, 128, "bf16", True, 0.5, 1234),
+}
 L2_FLUSH_BYTES = 256 << 20
 REFERENCE_UNAVAILABLE = (
     "the reference is a set of MPI programs (every source includes <mpi.h>) with no Python "
@@ -53,8 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--seq", type=int, default=SEQ_PER_RANK, help="tokens per rank")
-    ap.add_argument("--dtype", choices=("fp32", "bf16"), default="fp32")
+    ap.add_argument("--preset", choices=tuple(PRESETS), default="ref-fp32")
+    ap.add_argument("--seq", type=int, default=0, help="tokens per rank (0: preset)")
     ap.add_argument("--ring-mode", choices=("direct", "chain"), default="direct")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -90,9 +102,11 @@ def main() -> int:
     from ring_attention_benchmark_b200.models.oracle import attention_flops
     from ring_attention_benchmark_b200.utils.clocks import ClockSampler
 
-    attn = RingAttention(args.seq, HEADS, HEAD_DIM,
-                         dtype=torch.float32 if args.dtype == "fp32" else torch.bfloat16,
-                         ring_mode=args.ring_mode)
+    seq, heads, heads_kv, head_dim, dt, causal, mult, seed = PRESETS[args.preset]
+    seq = args.seq or seq
+    attn = RingAttention(seq, heads, head_dim, heads_kv=heads_kv,
+                         dtype=torch.float32 if dt == "fp32" else torch.bfloat16,
+                         causal=causal, zigzag=causal, ring_mode=args.ring_mode)
     rt = attn.runtime
     world, rank = rt.world, rt.rank
     if world != args.gpus:
@@ -100,7 +114,8 @@ def main() -> int:
         return 2
     dev = torch.device("cuda", rt.device)
     dtype = attn.dtype
-    x = inputs.normal_inputs(rank, args.seq, HEADS, HEAD_DIM)
+    x = inputs.normal_inputs(rank, seq, heads, head_dim, heads_kv=heads_kv,
+                             seed=None if seed is None else seed + rank, mult=mult)
     q = x.q.to(dev, dtype).contiguous()
     k = x.k.to(dev, dtype).contiguous()
     v = x.v.to(dev, dtype).contiguous()
@@ -108,8 +123,11 @@ def main() -> int:
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    flops_rank = attention_flops(args.seq, args.seq * world, HEADS, HEAD_DIM)
-    flops_total = flops_rank * world
+    total_tokens = seq * world
+    if causal:  # visible (query, key) pairs of a causal mask over the global sequence
+        flops_total = 4.0 * head_dim * heads * total_tokens * (total_tokens + 1) / 2
+    else:
+        flops_total = attention_flops(seq, total_tokens, heads, head_dim) * world
 
     # ---- warm-up ----
     for _ in range(args.warmup):
@@ -207,7 +225,7 @@ def main() -> int:
                "schedule": "copies of step i+1 overlap step i; K-step loop timed as a whole"}
 
     nsplit = attn.engine.nsplit
-    per_step = (2 if args.dtype == "fp32" else 0) + 1 + (1 if nsplit > 1 else 0)
+    per_step = (2 if dt == "fp32" else 0) + 1 + (1 if nsplit > 1 else 0)
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -220,18 +238,20 @@ def main() -> int:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "fp32" if args.dtype == "fp32" else "bf16",
+            "dtype": dt,
             "data": "synthetic",
             "config": {
-                "model": f"ring attention fwd, {HEADS} head, d={HEAD_DIM}, non-causal, "
-                         f"{'fp32 via 3xTF32 tensor-core products' if args.dtype == 'fp32' else 'bf16'}",
+                "model": (f"ring attention fwd [{args.preset}], {heads} q heads / {heads_kv} kv "
+                          f"heads, d={head_dim}, {'causal zigzag' if causal else 'non-causal'}, "
+                          f"{'fp32 via 3xTF32 tensor-core products' if dt == 'fp32' else 'bf16, fp32 accumulation'}"),
                 "global_batch": 1,
-                "seq_len": args.seq * world,
-                "seq_per_rank": args.seq,
-                "kv_block_elements_per_rank": args.seq * HEADS * HEAD_DIM,
+                "seq_len": total_tokens,
+                "seq_per_rank": seq,
+                "kv_block_elements_per_rank": seq * heads_kv * head_dim,
                 "parallelism": f"cp{world} (ring over NVLink, fused in-kernel transfer, "
                                f"{args.ring_mode} mode)",
-                "data_init": "iid N(0,1), seed=rank, scale 1/sqrt(64)",
+                "data_init": (f"iid N(0,1) x {mult}, seed={'rank' if seed is None else f'{seed}+rank'}, "
+                              f"scale 1/sqrt({head_dim})"),
                 "l2": "256 MiB buffer written between timed steps (outside the events)",
                 "flops_per_step_total": flops_total,
                 "wall_ms_bracketed_loop": round(wall_ms, 3),
