@@ -96,12 +96,20 @@ struct Item {
   int unit, chunk, h, hk, q0, v_begin, v_end;
 };
 
+// Query tile of a work unit.  With a causal mask the later query tiles see more
+// keys, so they are handed out first (longest-processing-time-first order
+// shortens the tail of the persistent schedule).
+__device__ __forceinline__ int unit_qtile(const FlashParams& p, int unit) {
+  const int qt = unit / p.Hq;
+  return p.causal ? (p.Sq / kM - 1 - qt) : qt;
+}
+
 __device__ __forceinline__ Item make_item(const FlashParams& p, int item, int tiles_total) {
   Item it;
   it.chunk = item / p.n_units;
   it.unit = item - it.chunk * p.n_units;
   it.h = it.unit % p.Hq;
-  const int qt = it.unit / p.Hq;
+  const int qt = unit_qtile(p, it.unit);
   it.hk = it.h / (p.Hq / p.Hkv);
   it.q0 = qt * kM;
   it.v_begin = static_cast<int>(static_cast<long long>(it.chunk) * tiles_total / p.nsplit);
@@ -683,7 +691,7 @@ __global__ void split_merge_kernel(const FlashParams p) {
   const int unit = static_cast<int>(urow / kM);
   const int row = static_cast<int>(urow % kM);
   const int h = unit % p.Hq;
-  const int qrow = (unit / p.Hq) * kM + row;
+  const int qrow = unit_qtile(p, unit) * kM + row;
   float mx = -INFINITY;
   for (int k = 0; k < p.nsplit; ++k)
     mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * kM + row]);
