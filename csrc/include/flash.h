@@ -44,7 +44,8 @@ struct FlashParams {
   int blk_offset;       // block s holds the keys of rank (rank - blk_offset - s) mod world
   // ---- work split ----
   int nsplit;           // KV chunks per (head, q tile) unit
-  int n_units;          // heads * q tiles
+  int rows_per_unit;    // query rows of one work unit (128, or 256 for the two-tile bf16 kernel)
+  int n_units;          // heads * Sq / rows_per_unit
   int n_items;          // n_units * nsplit
   // ---- outputs ----
   void* out;            // final O [Sq, Hq, D] (nsplit == 1 and !partial)
@@ -92,6 +93,11 @@ int flash_choose_split(int units, int tiles_per_unit, int sms);
 
 int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps, int grid,
                          bool cooperative, cudaStream_t stream);
+
+// Two-query-tile bf16 kernel (256-row work units); q map from flash_make_q_map.
+CUtensorMap flash_make_q_map(const void* q, int Sq, int Hq, int D);
+int flash_forward_2q_launch(const FlashParams& p, const CUtensorMap& tmq, const FlashMaps& maps,
+                            int grid, bool cooperative, cudaStream_t stream);
 
 // Merge nsplit partials of every unit into the final output (and LSE).
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream);
@@ -150,6 +156,7 @@ struct FlashArgs {
 };
 
 struct FlashPlan {
+  int rows_per_unit;  // 128 (one query tile per CTA) or 256 (two-tile bf16 kernel)
   int nsplit;
   int n_units;
   int n_items;

@@ -1,0 +1,175 @@
+// flash_common.cuh - pieces shared by the sm_100a flash-attention kernels:
+// work-item decomposition, causal tile classification by global position, the
+// cross-GPU flag primitives and the in-kernel ring copy role of the fused mode.
+#pragma once
+
+#include <cstdint>
+
+#include "flash.h"
+#include "sm100.cuh"
+
+namespace rab {
+namespace flash_detail {
+
+using namespace sm100;
+
+constexpr int kM = 128;                    // rows of one query tile (TMEM lanes)
+constexpr float kRescaleThreshold = 8.0f;  // lazy rescale threshold, log2 units
+constexpr float kLn2 = 0.69314718055994530942f;
+
+struct Item {
+  int unit, chunk, h, hk, q0, v_begin, v_end;
+};
+
+// First query row of a work unit.  Units run head-major (all query tiles of a
+// head, then the next head), so the CTAs of one wave share a head's K/V in L2.
+// With a causal mask the later query tiles see more keys; they are handed out
+// first (longest-processing-time-first shortens the tail of the schedule).
+__device__ __forceinline__ int unit_q0(const FlashParams& p, int unit) {
+  const int per_head = p.Sq / p.rows_per_unit;
+  const int qt = unit % per_head;
+  return (p.causal ? (per_head - 1 - qt) : qt) * p.rows_per_unit;
+}
+
+__device__ __forceinline__ int unit_head(const FlashParams& p, int unit) {
+  return unit / (p.Sq / p.rows_per_unit);
+}
+
+__device__ __forceinline__ Item make_item(const FlashParams& p, int item, int tiles_total) {
+  Item it;
+  it.chunk = item / p.n_units;
+  it.unit = item - it.chunk * p.n_units;
+  it.h = unit_head(p, it.unit);
+  it.hk = it.h / (p.Hq / p.Hkv);
+  it.q0 = unit_q0(p, it.unit);
+  it.v_begin = static_cast<int>(static_cast<long long>(it.chunk) * tiles_total / p.nsplit);
+  it.v_end = static_cast<int>(static_cast<long long>(it.chunk + 1) * tiles_total / p.nsplit);
+  return it;
+}
+
+__device__ __forceinline__ int global_pos(int local, int owner, int S, int W, int zigzag) {
+  if (!zigzag) return owner * S + local;
+  const int C = S >> 1;
+  return local < C ? owner * C + local : (2 * W - 1 - owner) * C + (local - C);
+}
+
+// Tile classification for the 128-row query tile starting at local row q0:
+// 0 = skip (fully masked), 1 = full, 2 = diagonal (mask per element).
+__device__ __forceinline__ int classify(const FlashParams& p, int q0, int v, int kN, int tpb,
+                                        int* k_lo_out, int* q_lo_out) {
+  if (!p.causal) return 1;
+  const int s = v / tpb, t = v - (v / tpb) * tpb;
+  const int owner = ((p.rank - p.blk_offset - s) % p.world + p.world) % p.world;
+  const int q_lo = global_pos(q0, p.rank, p.Sq, p.world, p.zigzag);
+  const int q_hi = q_lo + kM - 1;
+  const int k_lo = global_pos(t * kN, owner, p.Skv, p.world, p.zigzag);
+  const int k_hi = k_lo + kN - 1;
+  *k_lo_out = k_lo;
+  *q_lo_out = q_lo;
+  if (k_lo > q_hi) return 0;
+  if (k_hi <= q_lo) return 1;
+  return 2;
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Bounded poll of a 64-bit flag until it reaches `target`.
+__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, bool sys,
+                                          DeviceStatus* st, uint32_t where, uint32_t detail,
+                                          uint64_t timeout_ns) {
+  if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
+    if (st_read_error(st) != 0) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      st_record_timeout(st, where, detail);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// The fused mode's copy role, run by 64 threads (two warps) of every CTA:
+// slice blockIdx.x of every ring block 1..nblk-1 is pulled from peer memory
+// into this rank's slot; see FlashParams for the flag protocol.  `s_copy_ok`
+// is a shared word that makes each go / no-go decision uniform across the 64
+// threads before the named barrier they share.
+__device__ __forceinline__ void ring_copy_role(const FlashParams& p, int ct, int* s_copy_ok) {
+  DeviceStatus* st = p.status;
+  const uint64_t tmo = p.timeout_ns;
+  if (blockIdx.x == 0 && ct == 0) st_release_sys(p.flags_local + kFlagSlot0Ready, p.epoch);
+  const int left = (p.rank - 1 + p.world) % p.world;
+  const size_t n16 = p.slot_bytes / 16;
+  const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
+  const size_t beg = per * blockIdx.x;
+  const size_t end = beg + per < n16 ? beg + per : n16;
+  bool ok = true;
+  for (int s = 1; s < p.nblk && ok; ++s) {
+    const uint4* src;
+    uint64_t* src_flags;
+    if (p.ring_chain) {
+      src = reinterpret_cast<const uint4*>(p.peer_slots[left] + (size_t)(s - 1) * p.slot_bytes);
+      src_flags = p.flags_peer[left];
+    } else {
+      const int origin = ((p.rank - s) % p.world + p.world) % p.world;
+      src = reinterpret_cast<const uint4*>(p.peer_slots[origin]);
+      src_flags = p.flags_peer[origin];
+    }
+    if (ct == 0) {
+      bool w;
+      if (p.ring_chain && s > 1)
+        w = wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true, st,
+                      kSitePeerReady, s, tmo);
+      else
+        w = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, s, tmo);
+      *s_copy_ok = (w && st_read_error(st) == 0) ? 1 : 0;
+    }
+    named_bar_sync(1, 64);
+    ok = *s_copy_ok != 0;  // one decision for all 64 copy threads
+    if (!ok) break;
+    uint4* dst = reinterpret_cast<uint4*>(p.local_slots + (size_t)s * p.slot_bytes);
+    size_t i = beg + ct;
+    constexpr int U = 8;
+    for (; i + (U - 1) * 64 < end; i += U * 64) {
+      uint4 r[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) r[u] = __ldcg(src + i + u * 64);
+#pragma unroll
+      for (int u = 0; u < U; ++u) __stcg(dst + i + u * 64, r[u]);
+    }
+    for (; i < end; i += 64) __stcg(dst + i, __ldcg(src + i));
+    fence_proxy_async_global();
+    __threadfence_system();
+    named_bar_sync(1, 64);
+    if (ct == 0) {
+      red_add_release_sys(p.flags_local + kFlagArrivedBase + s, 1);
+      red_add_release_sys(src_flags + kFlagReads, 1);
+    }
+  }
+  // this rank's slots must outlive every peer's reads of this launch
+  if (ok && blockIdx.x == 0 && ct == 0)
+    wait_flag(p.flags_local + kFlagReads, p.reads_target, true, st, kSitePeerConsumed, 0, tmo);
+}
+
+}  // namespace flash_detail
+}  // namespace rab

@@ -6,14 +6,15 @@
 // per-step merge of the reference (src/attention/ring_attention_nccl_gpu_bench.cu
 // :341-348, kernels C16 + C17) disappears into the running rescale.
 //
-// CTA = 8 warps, one 128-row query tile of one head at a time (persistent over
-// work items):
+// CTA = 12 warps, one 128-row query tile of one head at a time (persistent
+// over work items):
 //   warp 0      TMA producer: K / V tiles of the ring slots -> shared memory
 //   warp 1      MMA issuer (one thread): S = Q K^T and O += P V on tcgen05,
 //               commits to mbarriers; also owns the TMEM allocation
 //   warps 2-3   ring copy warps (fused mode): peer slot -> local slot
-//   warps 4-7   softmax: one thread per query row; S and O live in TMEM,
-//               P is written back over S (A operand of the PV MMA from TMEM)
+//   warps 4-11  softmax, two warpgroups: each thread owns one query row and
+//               one half of the key columns; S and O live in TMEM, P is
+//               written back over S (A operand of the PV MMA from TMEM)
 //
 // Precisions:
 //   kBF16   bf16 Q/K/V, kind::f16, fp32 accumulation, bf16 P.
@@ -40,23 +41,22 @@
 #include <string>
 
 #include "flash.h"
+#include "flash_common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
 
 namespace rab {
 
 using namespace sm100;
+using namespace flash_detail;
 
 namespace {
 
-constexpr int kM = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;  // 12 warps
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpComm = 2;      // warps 2 and 3
-constexpr int kWarpSoftmax = 4;   // warps 4..7
-constexpr float kRescaleThreshold = 8.0f;
-constexpr float kLn2 = 0.69314718055994530942f;
+constexpr int kWarpSoftmax = 4;   // warps 4..11 (two warpgroups)
 constexpr uint32_t kTmemCols = 512;
 
 template <Prec P, int D>
@@ -72,7 +72,7 @@ struct Cfg {
   static constexpr int kVTile = kKTile;
   static constexpr int kStages = (kKTile + kVTile) <= 32768 ? 4 : 3;
   static constexpr int kSmemTiles = kStages * (kKTile + kVTile);
-  static constexpr int kNumBars = 4 * kStages + 8;
+  static constexpr int kNumBars = 4 * kStages + 12;
   static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
   // TMEM columns
   static constexpr uint32_t kColQ = 0;                       // Q (tf32: Qb at 0, Qs at D)
@@ -91,92 +91,6 @@ struct Cfg {
                                                   kTF32 ? kFmtTF32 : kFmtBF16, kM, D, kMajorK,
                                                   kTF32 ? kMajorK : kMajorMN);
 };
-
-struct Item {
-  int unit, chunk, h, hk, q0, v_begin, v_end;
-};
-
-// Query tile of a work unit.  With a causal mask the later query tiles see more
-// keys, so they are handed out first (longest-processing-time-first order
-// shortens the tail of the persistent schedule).
-__device__ __forceinline__ int unit_qtile(const FlashParams& p, int unit) {
-  const int qt = unit / p.Hq;
-  return p.causal ? (p.Sq / kM - 1 - qt) : qt;
-}
-
-__device__ __forceinline__ Item make_item(const FlashParams& p, int item, int tiles_total) {
-  Item it;
-  it.chunk = item / p.n_units;
-  it.unit = item - it.chunk * p.n_units;
-  it.h = it.unit % p.Hq;
-  const int qt = unit_qtile(p, it.unit);
-  it.hk = it.h / (p.Hq / p.Hkv);
-  it.q0 = qt * kM;
-  it.v_begin = static_cast<int>(static_cast<long long>(it.chunk) * tiles_total / p.nsplit);
-  it.v_end = static_cast<int>(static_cast<long long>(it.chunk + 1) * tiles_total / p.nsplit);
-  return it;
-}
-
-__device__ __forceinline__ int global_pos(int local, int owner, int S, int W, int zigzag) {
-  if (!zigzag) return owner * S + local;
-  const int C = S >> 1;
-  return local < C ? owner * C + local : (2 * W - 1 - owner) * C + (local - C);
-}
-
-// Tile classification: 0 = skip (fully masked), 1 = full, 2 = diagonal (mask per element)
-__device__ __forceinline__ int classify(const FlashParams& p, const Item& it, int v, int kN,
-                                        int tpb, int* k_lo_out, int* q_lo_out) {
-  if (!p.causal) return 1;
-  const int s = v / tpb, t = v - (v / tpb) * tpb;
-  const int owner = ((p.rank - p.blk_offset - s) % p.world + p.world) % p.world;
-  const int q_lo = global_pos(it.q0, p.rank, p.Sq, p.world, p.zigzag);
-  const int q_hi = q_lo + kM - 1;
-  const int k_lo = global_pos(t * kN, owner, p.Skv, p.world, p.zigzag);
-  const int k_hi = k_lo + kN - 1;
-  *k_lo_out = k_lo;
-  *q_lo_out = q_lo;
-  if (k_lo > q_hi) return 0;
-  if (k_hi <= q_lo) return 1;
-  return 2;
-}
-
-__device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void red_add_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Bounded poll of a 64-bit flag until it reaches `target`.
-__device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target, bool sys,
-                                          DeviceStatus* st, uint32_t where, uint32_t detail,
-                                          uint64_t timeout_ns) {
-  if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    __nanosleep(64);
-    if ((sys ? ld_acquire_sys(flag) : ld_acquire_gpu(flag)) >= target) return true;
-    if (st_read_error(st) != 0) return false;
-    if (globaltimer_ns() - t0 > timeout_ns) {
-      st_record_timeout(st, where, detail);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
 
 template <Prec P, int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -201,8 +115,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_full = bars + 4 * NS + 5;
   uint64_t* o_final = bars + 4 * NS + 6;
   uint64_t* drain = bars + 4 * NS + 7;
+  uint64_t* xbar = bars + 4 * NS + 8;   // [2] row-max exchange between the softmax halves
+  uint64_t* lbar = bars + 4 * NS + 10;  // [2] row-sum exchange
   __shared__ uint32_t tmem_slot;
   __shared__ int s_copy_ok;
+  __shared__ float s_xmax[2][2][kM];  // [tile parity][half][row] partial row maxima
+  __shared__ float s_xl[2][2][kM];    // [item parity][half][row] partial row sums
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -218,12 +136,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(&p_full[0], 128);
-    mbar_init(&p_full[1], 128);
+    mbar_init(&p_full[0], 256);
+    mbar_init(&p_full[1], 256);
     mbar_init(pv_done, 1);
-    mbar_init(q_full, 128);
+    mbar_init(q_full, 256);
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&xbar[i], 256);
+      mbar_init(&lbar[i], 256);
+    }
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
@@ -249,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Item it = make_item(p, item, tiles_total);
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
-          if (classify(p, it, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if (classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
@@ -358,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
-          if (classify(p, it, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if (classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
           const int stage = g % NS;
           const int b = g & 1;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
@@ -407,68 +329,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpComm || warp == kWarpComm + 1) {
     // ------------------------------------------------------------ ring copy
-    if (p.fused && p.world > 1) {
-      const int ct = threadIdx.x - kWarpComm * 32;  // 0..63
-      if (blockIdx.x == 0 && ct == 0)
-        st_release_sys(p.flags_local + kFlagSlot0Ready, p.epoch);
-      const int left = (p.rank - 1 + p.world) % p.world;
-      const size_t n16 = p.slot_bytes / 16;
-      const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
-      const size_t beg = per * blockIdx.x;
-      const size_t end = beg + per < n16 ? beg + per : n16;
-      bool ok = true;
-      for (int s = 1; s < p.nblk && ok; ++s) {
-        const uint4* src;
-        uint64_t* src_flags;
-        if (p.ring_chain) {
-          src = reinterpret_cast<const uint4*>(p.peer_slots[left] + (size_t)(s - 1) * p.slot_bytes);
-          src_flags = p.flags_peer[left];
-        } else {
-          const int origin = ((p.rank - s) % p.world + p.world) % p.world;
-          src = reinterpret_cast<const uint4*>(p.peer_slots[origin]);
-          src_flags = p.flags_peer[origin];
-        }
-        if (ct == 0) {
-          bool w;
-          if (p.ring_chain && s > 1)
-            w = wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true, st,
-                          kSitePeerReady, s, tmo);
-          else
-            w = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, s, tmo);
-          s_copy_ok = (w && st_read_error(st) == 0) ? 1 : 0;
-        }
-        named_bar_sync(1, 64);
-        ok = s_copy_ok != 0;  // one decision for all 64 copy threads
-        if (!ok) break;
-        uint4* dst = reinterpret_cast<uint4*>(p.local_slots + (size_t)s * p.slot_bytes);
-        size_t i = beg + ct;
-        constexpr int U = 8;
-        for (; i + (U - 1) * 64 < end; i += U * 64) {
-          uint4 r[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) r[u] = __ldcg(src + i + u * 64);
-#pragma unroll
-          for (int u = 0; u < U; ++u) __stcg(dst + i + u * 64, r[u]);
-        }
-        for (; i < end; i += 64) __stcg(dst + i, __ldcg(src + i));
-        fence_proxy_async_global();
-        __threadfence_system();
-        named_bar_sync(1, 64);
-        if (ct == 0) {
-          red_add_release_sys(p.flags_local + kFlagArrivedBase + s, 1);
-          red_add_release_sys(src_flags + kFlagReads, 1);
-        }
-      }
-      // this rank's slots must outlive every peer's reads of this launch
-      if (ok && blockIdx.x == 0 && ct == 0)
-        wait_flag(p.flags_local + kFlagReads, p.reads_target, true, st, kSitePeerConsumed, 0,
-                  tmo);
-    }
+    if (p.fused && p.world > 1) ring_copy_role(p, threadIdx.x - kWarpComm * 32, &s_copy_ok);
   } else {
     // -------------------------------------------------------------- softmax
-    const int row = threadIdx.x - kWarpSoftmax * 32;   // 0..127, TMEM lane
-    const uint32_t wq = warp & 3;                      // TMEM sub-partition
-    const uint32_t lane_base = (wq * 32) << 16;
+    // Two warpgroups per query tile: warpgroup `half` owns the S (and P)
+    // columns [half*kN/2, (half+1)*kN/2) and the Q / O columns
+    // [half*D/2, (half+1)*D/2) of all 128 rows.  The row max is exchanged
+    // through shared memory each tile; the partial row sums are combined once
+    // per work item.  Two softmax warps per SM sub-partition keep the exp /
+    // conversion pipe and the tensor pipe busy at the same time.
+    constexpr int kHalfN = kN / 2;
+    constexpr int kHalfD = D / 2;
+    const int sm_t = threadIdx.x - kWarpSoftmax * 32;  // 0..255
+    const int half = sm_t >> 7;
+    const int row = sm_t & 127;                          // TMEM lane
+    const uint32_t lane_base = ((warp & 3) * 32) << 16;
     const float sl2 = p.scale_log2;
     int g = 0;
     int item_count = 0;
@@ -477,88 +352,99 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
       const Item it = make_item(p, item, tiles_total);
       const int qrow = it.q0 + row;
-      // ---- Q -> TMEM ----
+      // ---- this warpgroup's half of the Q row -> TMEM ----
       {
         if constexpr (C::kTF32) {
           const float4* qp = reinterpret_cast<const float4*>(
-              static_cast<const float*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D);
+              static_cast<const float*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D +
+              half * kHalfD);
           uint32_t big[32], small[32];
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 x = __ldg(qp + c / 4 + i);
-              split_tf32_alu(x.x, big[4 * i + 0], small[4 * i + 0]);
-              split_tf32_alu(x.y, big[4 * i + 1], small[4 * i + 1]);
-              split_tf32_alu(x.z, big[4 * i + 2], small[4 * i + 2]);
-              split_tf32_alu(x.w, big[4 * i + 3], small[4 * i + 3]);
-            }
-            tmem_st32(tmem + lane_base + C::kColQ + c, big);
-            tmem_st32(tmem + lane_base + C::kColQ + C::kQCols + c, small);
+          for (int i = 0; i < 8; ++i) {
+            const float4 x = __ldg(qp + i);
+            split_tf32_alu(x.x, big[4 * i + 0], small[4 * i + 0]);
+            split_tf32_alu(x.y, big[4 * i + 1], small[4 * i + 1]);
+            split_tf32_alu(x.z, big[4 * i + 2], small[4 * i + 2]);
+            split_tf32_alu(x.w, big[4 * i + 3], small[4 * i + 3]);
           }
+          tmem_st32(tmem + lane_base + C::kColQ + half * kHalfD, big);
+          tmem_st32(tmem + lane_base + C::kColQ + C::kQCols + half * kHalfD, small);
         } else {
+          constexpr int kQc = D / 4;  // packed bf16 columns per warpgroup
           const uint4* qp = reinterpret_cast<const uint4*>(
-              static_cast<const uint16_t*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D);
+              static_cast<const uint16_t*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D +
+              half * kHalfD);
           uint32_t w[32];
 #pragma unroll
-          for (int c = 0; c < D / 2; c += 32) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const uint4 x = __ldg(qp + c / 4 + i);
-              w[4 * i + 0] = x.x;
-              w[4 * i + 1] = x.y;
-              w[4 * i + 2] = x.z;
-              w[4 * i + 3] = x.w;
-            }
-            tmem_st32(tmem + lane_base + C::kColQ + c, w);
+          for (int i = 0; i < kQc / 4; ++i) {
+            const uint4 x = __ldg(qp + i);
+            w[4 * i + 0] = x.x;
+            w[4 * i + 1] = x.y;
+            w[4 * i + 2] = x.z;
+            w[4 * i + 3] = x.w;
           }
+          if constexpr (kQc == 32)
+            tmem_st32(tmem + lane_base + C::kColQ + half * kQc, w);
+          else
+            tmem_st16(tmem + lane_base + C::kColQ + half * kQc, w);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(q_full);
       }
-      float m_run = -INFINITY;  // running max of scaled log2 scores
-      float l_run = 0.f;
+      float m_run = -INFINITY;  // running max of scaled log2 scores (same in both halves)
+      float l_part = 0.f;       // this half's share of the row sum
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
         int k_lo = 0, q_lo = 0;
-        const int cls = classify(p, it, v, kN, tpb, &k_lo, &q_lo);
+        const int cls = classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo);
         if (cls == 0) continue;
         const int b = g & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo));
         if (!ok) break;
         tc_fence_after();
         const uint32_t s_tm = tmem + lane_base + (b ? C::kColS1 : C::kColS0);
-        uint32_t sr[kN];
+        uint32_t sr[kHalfN];
 #pragma unroll
-        for (int c = 0; c < kN; c += 32) tmem_ld32(s_tm + c, sr + c);
+        for (int c = 0; c < kHalfN; c += 32) tmem_ld32(s_tm + half * kHalfN + c, sr + c);
         tmem_ld_wait();
         if (cls == 2) {
-          const int lim = q_lo + row - k_lo;  // key index c visible iff c <= lim
+          const int lim = q_lo + row - k_lo - half * kHalfN;  // column c visible iff c <= lim
 #pragma unroll
-          for (int c = 0; c < kN; ++c)
+          for (int c = 0; c < kHalfN; ++c)
             if (c > lim) sr[c] = 0xff800000u;  // -inf
         }
-        float mx = __uint_as_float(sr[0]);
+        float pm[8];
 #pragma unroll
-        for (int c = 1; c < kN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-        mx *= sl2;
+        for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sr[i]);
+#pragma unroll
+        for (int c = 8; c < kHalfN; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
+        const float mx_part = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                    fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        s_xmax[g & 1][half][row] = mx_part;
+        // bounded exchange (an mbarrier, not bar.sync): if the other half gave
+        // up on an error this wait runs out instead of hanging
+        mbar_arrive(&xbar[g & 1]);
+        ok = __all_sync(0xffffffffu, mbar_wait(&xbar[g & 1], (g >> 1) & 1, st, kSiteSFull, tmo));
+        if (!ok) break;
+        const float mx = fmaxf(mx_part, s_xmax[g & 1][half ^ 1][row]) * sl2;
         // lazy rescale: move the reference max only when it grows by > 2^8
+        // (both halves see the same mx and m_run, so they decide alike)
         const bool need = mx > m_run + kRescaleThreshold;
         float alpha = 1.f;
         if (need) {
           alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - mx);
           m_run = mx;
-          l_run *= alpha;
+          l_part *= alpha;
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // O holds PV of earlier tiles: wait until the last PV landed, then scale rows
           ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (g - 1) & 1, st, kSitePvDone, tmo));
           if (!ok) break;
           tc_fence_after();
-          const uint32_t o_tm = tmem + lane_base + C::kColO;
+          const uint32_t o_tm = tmem + lane_base + C::kColO + half * kHalfD;
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
+          for (int c = 0; c < kHalfD; c += 32) {
             uint32_t o[32];
             tmem_ld32(o_tm + c, o);
             tmem_ld_wait();
@@ -568,35 +454,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float rowsum = 0.f;
+        float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
         if constexpr (C::kTF32) {
-          uint32_t pb[32], ps[32];
+          uint32_t pb[32], psm[32];
 #pragma unroll
-          for (int c = 0; c < kN; c += 32) {
+          for (int c = 0; c < kHalfN; c += 32) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float e = ex2_approx(fmaf(__uint_as_float(sr[c + i]), sl2, -m_use));
-              rowsum += e;
-              split_tf32_alu(e, pb[i], ps[i]);
+              ps8[i & 7] += e;
+              split_tf32_alu(e, pb[i], psm[i]);
             }
-            tmem_st32(s_tm + c, pb);
-            tmem_st32(tmem + lane_base + (b ? C::kColPs1 : C::kColPs0) + c, ps);
+            tmem_st32(s_tm + half * kHalfN + c, pb);
+            tmem_st32(tmem + lane_base + (b ? C::kColPs1 : C::kColPs0) + half * kHalfN + c, psm);
           }
         } else {
           uint32_t pk[32];
 #pragma unroll
-          for (int c = 0; c < kN; c += 64) {
+          for (int c = 0; c < kHalfN; c += 64) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i]), sl2, -m_use));
               const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i + 1]), sl2, -m_use));
-              rowsum += e0 + e1;
+              ps8[i & 7] += e0 + e1;
               pk[i] = pack_bf16x2(e0, e1);
             }
-            tmem_st32(s_tm + c / 2, pk);
+            tmem_st32(s_tm + (half * kHalfN + c) / 2, pk);
           }
         }
-        l_run += rowsum;
+        l_part += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[b]);
@@ -604,7 +490,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++g;
       }
       if (!ok) break;
-      // ---- epilogue ----
+      // ---- combine the two halves' row sums ----
+      s_xl[item_count & 1][half][row] = l_part;
+      mbar_arrive(&lbar[item_count & 1]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&lbar[item_count & 1], (item_count >> 1) & 1, st,
+                                             kSiteOReady, tmo));
+      if (!ok) break;
+      const float l_run = l_part + s_xl[item_count & 1][half ^ 1][row];
+      // ---- epilogue: this half's columns of O ----
       const bool have = j > 0;
       if (have) {
         ok = __all_sync(0xffffffffu, mbar_wait(o_final, final_count & 1, st, kSiteOReady, tmo));
@@ -612,20 +505,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      const uint32_t o_tm = tmem + lane_base + C::kColO;
+      const uint32_t o_tm = tmem + lane_base + C::kColO + half * kHalfD;
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
       const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
       const bool split = p.nsplit > 1;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
       float* dst_f32 = nullptr;
       if (split)
-        dst_f32 = p.split_acc + (static_cast<size_t>(item) * kM + row) * D;
+        dst_f32 = p.split_acc + (static_cast<size_t>(item) * kM + row) * D + half * kHalfD;
       else if (p.partial)
-        dst_f32 = p.acc + r * D;
+        dst_f32 = p.acc + r * D + half * kHalfD;
       else if (!p.out_bf16)
-        dst_f32 = static_cast<float*>(p.out) + r * D;
+        dst_f32 = static_cast<float*>(p.out) + r * D + half * kHalfD;
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int c = 0; c < kHalfD; c += 32) {
         uint32_t o[32];
         if (have) {
           tmem_ld32(o_tm + c, o);
@@ -642,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 __uint_as_float(o[4 * i + 2]) * inv,
                                 __uint_as_float(o[4 * i + 3]) * inv);
         } else {
-          uint4* d4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + r * D + c);
+          uint4* d4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + r * D +
+                                               half * kHalfD + c);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv,
@@ -655,20 +549,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
-      if (split) {
-        p.split_m[static_cast<size_t>(item) * kM + row] = m_nat;
-        p.split_l[static_cast<size_t>(item) * kM + row] = l_run;
-      } else if (p.partial) {
-        if (p.m_out) p.m_out[r] = m_nat;
-        if (p.l_out) p.l_out[r] = l_run;
-      } else if (p.lse != nullptr) {
-        p.lse[r] = (have && l_run > 0.f) ? m_nat + logf(l_run) : -INFINITY;
+      if (half == 0) {
+        if (split) {
+          p.split_m[static_cast<size_t>(item) * kM + row] = m_nat;
+          p.split_l[static_cast<size_t>(item) * kM + row] = l_run;
+        } else if (p.partial) {
+          if (p.m_out) p.m_out[r] = m_nat;
+          if (p.l_out) p.l_out[r] = l_run;
+        } else if (p.lse != nullptr) {
+          p.lse[r] = (have && l_run > 0.f) ? m_nat + logf(l_run) : -INFINITY;
+        }
       }
       // all TMEM reads of this item are done before the next Q lands in TMEM
       tc_fence_before();
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == kWarpMma) {
@@ -684,26 +579,27 @@ template <int D>
 __global__ void split_merge_kernel(const FlashParams p) {
   constexpr int kTpr = D / 4;
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  const long long rows_total = static_cast<long long>(p.n_units) * kM;
+  const int R = p.rows_per_unit;
+  const long long rows_total = static_cast<long long>(p.n_units) * R;
   const long long urow = t / kTpr;
   const int c = static_cast<int>(t % kTpr);
   if (urow >= rows_total) return;
-  const int unit = static_cast<int>(urow / kM);
-  const int row = static_cast<int>(urow % kM);
-  const int h = unit % p.Hq;
-  const int qrow = unit_qtile(p, unit) * kM + row;
+  const int unit = static_cast<int>(urow / R);
+  const int row = static_cast<int>(urow % R);
+  const int h = unit_head(p, unit);
+  const int qrow = unit_q0(p, unit) + row;
   float mx = -INFINITY;
   for (int k = 0; k < p.nsplit; ++k)
-    mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * kM + row]);
+    mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * R + row]);
   const float mref = (mx == -INFINITY) ? 0.f : mx;
   float l = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < p.nsplit; ++k) {
     const size_t it = static_cast<size_t>(k) * p.n_units + unit;
-    const float mk = p.split_m[it * kM + row];
+    const float mk = p.split_m[it * R + row];
     const float w = (mk == -INFINITY) ? 0.f : expf(mk - mref);
-    l += w * p.split_l[it * kM + row];
-    const float4 x = reinterpret_cast<const float4*>(p.split_acc + (it * kM + row) * D)[c];
+    l += w * p.split_l[it * R + row];
+    const float4 x = reinterpret_cast<const float4*>(p.split_acc + (it * R + row) * D)[c];
     a.x += w * x.x;
     a.y += w * x.y;
     a.z += w * x.z;
@@ -899,7 +795,7 @@ int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps,
 }
 
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream) {
-  const long long threads_total = static_cast<long long>(p.n_units) * kM * (p.D / 4);
+  const long long threads_total = static_cast<long long>(p.n_units) * p.rows_per_unit * (p.D / 4);
   const int bs = 256;
   const int blocks = static_cast<int>((threads_total + bs - 1) / bs);
   if (p.D == 64)

@@ -108,6 +108,7 @@ extern "C" int rab_flash_attention_noalloc(const void* q, const void* k, const v
     p.causal = causal ? 1 : 0;
     p.world = 1;
     p.nsplit = ns;
+    p.rows_per_unit = 128;  // one query tile per work unit
     p.n_units = units;
     p.n_items = items;
     p.out = out;

@@ -2,6 +2,7 @@
 // workspace and cached tensor maps.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -30,13 +31,23 @@ const FlashMaps& cached_maps(Prec prec, const void* k, const void* v, size_t str
   return cache.emplace(key, flash_make_maps(prec, k, v, stride, nblk, Skv, Hkv, D)).first->second;
 }
 
+// The two-query-tile bf16 kernel is opt-in (RAB_FLASH_2Q=1): measured on B200
+// it trails the one-tile kernel, whose head-major work order already keeps
+// the tensor and exp pipes equally busy.
+bool two_tile_enabled() {
+  const char* e = std::getenv("RAB_FLASH_2Q");
+  return e != nullptr && std::strcmp(e, "1") == 0;
+}
+
 }  // namespace
 
 FlashPlan flash_plan(const FlashArgs& a) {
   if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
   FlashPlan pl;
   const int kN = a.prec == Prec::kF32x3 ? 64 : 128;
-  pl.n_units = a.Hq * (a.Sq / 128);
+  // bf16 may use the two-query-tile kernel when the rows split into 256-row units
+  pl.rows_per_unit = (a.prec == Prec::kBF16 && a.Sq % 256 == 0 && two_tile_enabled()) ? 256 : 128;
+  pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
   const int tiles = a.nblk * (a.Skv / kN);
   const int sms = flash_sm_count();
   pl.nsplit = a.nsplit > 0 ? a.nsplit : flash_choose_split(pl.n_units, tiles, sms);
@@ -44,8 +55,9 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.n_items = pl.n_units * pl.nsplit;
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
   if (a.fused) pl.grid = a.grid > 0 ? a.grid : sms;  // every CTA also copies a slice
-  pl.workspace_bytes =
-      pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * 128 * (a.D + 2) * sizeof(float) : 0;
+  pl.workspace_bytes = pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * pl.rows_per_unit *
+                                           (a.D + 2) * sizeof(float)
+                                     : 0;
   return pl;
 }
 
@@ -68,6 +80,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.rank = a.rank;
   p.blk_offset = a.blk_offset;
   p.nsplit = pl.nsplit;
+  p.rows_per_unit = pl.rows_per_unit;
   p.n_units = pl.n_units;
   p.n_items = pl.n_items;
   p.out = a.out;
@@ -80,8 +93,8 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   if (pl.nsplit > 1) {
     float* ws = static_cast<float*>(a.workspace);
     p.split_acc = ws;
-    p.split_m = ws + static_cast<size_t>(pl.n_items) * 128 * a.D;
-    p.split_l = p.split_m + static_cast<size_t>(pl.n_items) * 128;
+    p.split_m = ws + static_cast<size_t>(pl.n_items) * pl.rows_per_unit * a.D;
+    p.split_l = p.split_m + static_cast<size_t>(pl.n_items) * pl.rows_per_unit;
   }
   p.fused = a.fused ? 1 : 0;
   p.ring_chain = a.ring_chain ? 1 : 0;
@@ -100,7 +113,13 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   if (p.status == nullptr) throw std::runtime_error("flash: a device status word is required");
   const FlashMaps& maps =
       cached_maps(a.prec, a.k_base, a.v_base, a.slot_stride, a.nblk, a.Skv, a.Hkv, a.D);
-  int err = flash_forward_launch(a.prec, p, maps, pl.grid, a.fused, stream);
+  int err;
+  if (pl.rows_per_unit == 256) {
+    const CUtensorMap tq = flash_make_q_map(a.q, a.Sq, a.Hq, a.D);
+    err = flash_forward_2q_launch(p, tq, maps, pl.grid, a.fused, stream);
+  } else {
+    err = flash_forward_launch(a.prec, p, maps, pl.grid, a.fused, stream);
+  }
   if (err != 0) return err;
   if (pl.nsplit > 1) err = flash_split_merge_launch(p, stream);
   return err;

@@ -101,3 +101,16 @@ def test_partial_contract_fp32(cuda_device):
     assert torch.allclose(out, racc / rl.unsqueeze(-1), atol=2e-5)
     assert torch.allclose(m.cpu().double() + torch.log(l.cpu().double()), rm + torch.log(rl),
                           atol=2e-5)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_two_tile_bf16_kernel(cuda_device, monkeypatch, causal):
+    """The opt-in two-query-tile bf16 kernel (RAB_FLASH_2Q=1) against the oracle."""
+    monkeypatch.setenv("RAB_FLASH_2Q", "1")
+    world = 2
+    qs, ks, vs = _blocks(world, 512, 4, 2, 128, torch.bfloat16, seed=5)
+    for rank in range(world):
+        out, lse = _run_rank(cuda_device, qs, ks, vs, rank, world, causal=causal, zigzag=causal)
+        ref, rlse = _oracle_rank(qs, ks, vs, rank, world, causal=causal, zigzag=causal)
+        assert (out.double() - ref).abs().max().item() < 2e-2
+        assert (lse.double() - rlse).abs().max().item() < 2e-2
