@@ -88,8 +88,9 @@ struct FlashMaps {
 FlashMaps flash_make_maps(Prec prec, const void* k_base, const void* v_base, size_t slot_stride,
                           int nblk, int Skv, int Hkv, int D);
 
-// Pick nsplit for `units` work units on `sms` SMs.
-int flash_choose_split(int units, int tiles_per_unit, int sms);
+// Pick nsplit for `units` work units of `tiles_per_unit` KV tiles on `sms` SMs,
+// with a fixed per-item overhead equivalent to `overhead_tiles` tiles.
+int flash_choose_split(int units, int tiles_per_unit, int sms, int overhead_tiles);
 
 int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps, int grid,
                          bool cooperative, cudaStream_t stream);

@@ -762,16 +762,20 @@ FlashMaps flash_make_maps(Prec prec, const void* k_base, const void* v_base, siz
   return m;
 }
 
-int flash_choose_split(int units, int tiles_per_unit, int sms) {
+int flash_choose_split(int units, int tiles_per_unit, int sms, int overhead_tiles) {
+  // Cost model fitted to B200 measurements of the fp32 kernel: a work item
+  // costs its KV tiles plus a fixed overhead (pipeline fill and drain, Q
+  // staging, epilogue, partial write-back) of about six 64-key tiles, and the
+  // persistent grid runs ceil(items / SMs) waves.
   int best = 1;
-  double best_eff = 0.0;
-  for (int c = 1; c <= 16; ++c) {
-    if (c > 1 && tiles_per_unit / c < 4) break;  // keep chunks long enough
+  double best_cost = 1e300;
+  for (int c = 1; c <= 16 && c <= tiles_per_unit; ++c) {
     const long long items = static_cast<long long>(units) * c;
     const long long waves = (items + sms - 1) / sms;
-    const double eff = static_cast<double>(items) / static_cast<double>(waves * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
+    const double cost = static_cast<double>(waves) *
+                        (static_cast<double>(tiles_per_unit) / c + overhead_tiles);
+    if (cost < best_cost * 0.995) {
+      best_cost = cost;
       best = c;
     }
   }

@@ -79,7 +79,7 @@ extern "C" int rab_flash_attention_noalloc(const void* q, const void* k, const v
   const int sms = flash_sm_count();
   const int units = Hq * (Sq / 128);
   const int tiles = Skv / 128;
-  int ns = nsplit > 0 ? nsplit : flash_choose_split(units, tiles, sms);
+  int ns = nsplit > 0 ? nsplit : flash_choose_split(units, tiles, sms, 3);
   if (ns > tiles) ns = tiles;
   const int items = units * ns;
   const size_t need = ns > 1 ? static_cast<size_t>(items) * 128 * (D + 2) * sizeof(float) : 0;

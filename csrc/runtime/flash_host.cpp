@@ -50,7 +50,9 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
   const int tiles = a.nblk * (a.Skv / kN);
   const int sms = flash_sm_count();
-  pl.nsplit = a.nsplit > 0 ? a.nsplit : flash_choose_split(pl.n_units, tiles, sms);
+  // per-item overhead in tiles: ~6 of the fp32 kernel's 64-key tiles, ~3 of 128-key bf16 tiles
+  pl.nsplit = a.nsplit > 0 ? a.nsplit
+                           : flash_choose_split(pl.n_units, tiles, sms, a.prec == Prec::kF32x3 ? 6 : 3);
   if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;
   pl.n_items = pl.n_units * pl.nsplit;
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
