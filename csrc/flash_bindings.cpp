@@ -95,7 +95,8 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
   const int err = flash_run(a, pl, cur_stream());
   TORCH_CHECK(err == 0, "flash_fwd launch failed: ",
               cudaGetErrorString(static_cast<cudaError_t>(err)));
-  return {pl.nsplit, pl.n_items, pl.grid};
+  // nsplit -1 reports the balanced schedule
+  return {pl.balanced ? -1 : pl.nsplit, pl.n_items, pl.grid};
 }
 
 }  // namespace

@@ -96,7 +96,7 @@ class FusedRing {
   uint8_t* slot0_k() const;  // bf16: raw K layout; write inputs here to skip the copy
   uint8_t* slot0_v() const;
   int grid() const { return plan_.grid; }
-  int nsplit() const { return plan_.nsplit; }
+  int nsplit() const { return plan_.balanced ? -1 : plan_.nsplit; }  // -1: balanced schedule
   uint64_t launches() const { return epoch_; }
 
  private:

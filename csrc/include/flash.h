@@ -43,10 +43,15 @@ struct FlashParams {
   int world, rank;
   int blk_offset;       // block s holds the keys of rank (rank - blk_offset - s) mod world
   // ---- work split ----
-  int nsplit;           // KV chunks per (head, q tile) unit
+  int nsplit;           // KV chunks per (head, q tile) unit (equal-split schedule)
+  int balanced;         // 1: balanced schedule: full_waves waves of whole units, then the
+                        //    remaining units' (unit, KV tile) space shared out evenly, CTA c
+                        //    owning tiles [c*T/G, (c+1)*T/G); needs causal == 0, 128-row units
+  int full_waves;       // balanced: whole-unit waves before the shared-out remainder
+  int kv_tiles;         // KV tiles of one unit over the whole ring (nblk * Skv / tile keys)
   int rows_per_unit;    // query rows of one work unit (128, or 256 for the two-tile bf16 kernel)
   int n_units;          // heads * Sq / rows_per_unit
-  int n_items;          // n_units * nsplit
+  int n_items;          // n_units * nsplit; balanced: the number of CTAs G
   // ---- outputs ----
   void* out;            // final O [Sq, Hq, D] (nsplit == 1 and !partial)
   int out_bf16;
@@ -55,9 +60,9 @@ struct FlashParams {
   float* acc;           // partial acc [Sq, Hq, D]     (partial, nsplit == 1)
   float* m_out;         // partial m [Sq, Hq]
   float* l_out;         // partial l [Sq, Hq]
-  float* split_acc;     // nsplit > 1: [n_items][128][D]
-  float* split_m;       // [n_items][128] (natural log)
-  float* split_l;       // [n_items][128]
+  float* split_acc;     // nsplit > 1: [n_items][128][D]; balanced: [2 * G][128][D]
+  float* split_m;       // [records][128] (natural log)
+  float* split_l;       // [records][128]
   // ---- fused ring transfer ----
   int fused;            // 1: copy blocks 1..nblk-1 from peers inside the kernel
   int ring_chain;       // 0: pull block s from its origin's slot 0; 1: from the left neighbour's slot s-1
@@ -92,6 +97,10 @@ FlashMaps flash_make_maps(Prec prec, const void* k_base, const void* v_base, siz
 // with a fixed per-item overhead equivalent to `overhead_tiles` tiles.
 int flash_choose_split(int units, int tiles_per_unit, int sms, int overhead_tiles);
 
+// True when the balanced schedule is expected to beat the best equal split
+// (same cost model; only valid without a causal mask).
+bool flash_prefer_balanced(int units, int tiles_per_unit, int sms, int overhead_tiles);
+
 int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps, int grid,
                          bool cooperative, cudaStream_t stream);
 
@@ -100,7 +109,8 @@ CUtensorMap flash_make_q_map(const void* q, int Sq, int Hq, int D);
 int flash_forward_2q_launch(const FlashParams& p, const CUtensorMap& tmq, const FlashMaps& maps,
                             int grid, bool cooperative, cudaStream_t stream);
 
-// Merge nsplit partials of every unit into the final output (and LSE).
+// Merge the split partials (nsplit > 1: every unit; balanced: the units a CTA
+// boundary cuts) into the final output (and LSE), or into acc/m/l when partial.
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream);
 
 // Ring-format preparation of one block: kF32x3 -> tf32 planes, V transposed.
@@ -137,7 +147,7 @@ struct FlashArgs {
   float* acc = nullptr;
   float* m = nullptr;
   float* l = nullptr;
-  int nsplit = 0;                    // <= 0: choose
+  int nsplit = 0;                    // > 0: equal split; 0: choose; -1: balanced schedule
   void* workspace = nullptr;         // split partials (see flash_workspace_bytes)
   size_t workspace_bytes = 0;
   int grid = 0;                      // <= 0: min(items, SMs)
@@ -158,7 +168,9 @@ struct FlashArgs {
 
 struct FlashPlan {
   int rows_per_unit;  // 128 (one query tile per CTA) or 256 (two-tile bf16 kernel)
-  int nsplit;
+  int nsplit;         // equal-split chunks per unit; 1 under the balanced schedule
+  int balanced;       // 1: balanced schedule (n_items == grid == CTAs)
+  int full_waves;     // balanced: whole-unit waves before the shared-out remainder
   int n_units;
   int n_items;
   int grid;

@@ -17,8 +17,12 @@ constexpr int kM = 128;                    // rows of one query tile (TMEM lanes
 constexpr float kRescaleThreshold = 8.0f;  // lazy rescale threshold, log2 units
 constexpr float kLn2 = 0.69314718055994530942f;
 
+// One work item: query tile `unit` (head h, first row q0) against the ring's
+// KV tiles [v_begin, v_end).  `store` is the index of the split partial record
+// the item writes (split_acc / split_m / split_l), or -1 when the item covers
+// every KV tile of its unit and writes the final result itself.
 struct Item {
-  int unit, chunk, h, hk, q0, v_begin, v_end;
+  int unit, h, hk, q0, v_begin, v_end, store;
 };
 
 // First query row of a work unit.  Units run head-major (all query tiles of a
@@ -35,15 +39,91 @@ __device__ __forceinline__ int unit_head(const FlashParams& p, int unit) {
   return unit / (p.Sq / p.rows_per_unit);
 }
 
+__device__ __forceinline__ void set_unit(const FlashParams& p, int unit, Item& it) {
+  it.unit = unit;
+  it.h = unit_head(p, unit);
+  it.hk = it.h / (p.Hq / p.Hkv);
+  it.q0 = unit_q0(p, unit);
+}
+
+// Equal-split schedule: item = chunk * n_units + unit, chunk in [0, nsplit).
 __device__ __forceinline__ Item make_item(const FlashParams& p, int item, int tiles_total) {
   Item it;
-  it.chunk = item / p.n_units;
-  it.unit = item - it.chunk * p.n_units;
-  it.h = unit_head(p, it.unit);
-  it.hk = it.h / (p.Hq / p.Hkv);
-  it.q0 = unit_q0(p, it.unit);
-  it.v_begin = static_cast<int>(static_cast<long long>(it.chunk) * tiles_total / p.nsplit);
-  it.v_end = static_cast<int>(static_cast<long long>(it.chunk + 1) * tiles_total / p.nsplit);
+  const int chunk = item / p.n_units;
+  set_unit(p, item - chunk * p.n_units, it);
+  it.v_begin = static_cast<int>(static_cast<long long>(chunk) * tiles_total / p.nsplit);
+  it.v_end = static_cast<int>(static_cast<long long>(chunk + 1) * tiles_total / p.nsplit);
+  it.store = p.nsplit > 1 ? item : -1;
+  return it;
+}
+
+// Balanced schedule (every KV tile costs the same, i.e. no causal mask).  The
+// first full_waves * G units run whole, unit blockIdx.x + k * G in wave k (the
+// head-major order of the equal-split schedule, which keeps the CTAs of a
+// wave on the same heads' K/V in L2).  The remaining R < G units are shared
+// out evenly: CTA c of G owns the tiles [c*T/G, (c+1)*T/G) of their (unit,
+// KV tile) space, T = R * tiles_total, cut at unit boundaries into pieces.  A
+// piece that is not a whole unit writes split record 2c (the piece holding
+// the range's first tile) or 2c+1 (the one holding its last tile), and
+// balanced_merge_kernel combines the records of each unit a CTA boundary cuts.
+__device__ __forceinline__ long long balanced_start(long long T, int G, int c) {
+  return static_cast<long long>(c) * T / G;
+}
+
+// Per-CTA work description, computed once by one thread into shared memory:
+// [0] work items, [1] whole-unit waves, [2] pieces n, [3] first piece's unit,
+// [4] rotation (1: the leading piece runs last), [5] first tile of the leading
+// piece, [6] end tile of the last piece.
+constexpr int kWorkWords = 7;
+
+__device__ __forceinline__ void work_setup(const FlashParams& p, int tiles_total, int* sw) {
+  if (!p.balanced) {
+    sw[0] = blockIdx.x < p.n_items ? (p.n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    return;
+  }
+  const int G = gridDim.x;
+  const int base = p.full_waves * G;
+  const long long T = static_cast<long long>(p.n_units - base) * tiles_total;
+  const long long s = balanced_start(T, G, blockIdx.x);
+  const long long e = balanced_start(T, G, blockIdx.x + 1);
+  sw[1] = p.full_waves;
+  if (e <= s) {
+    sw[0] = p.full_waves;
+    sw[2] = 0;
+    return;
+  }
+  const int u_lo = static_cast<int>(s / tiles_total);
+  const int u_hi = static_cast<int>((e - 1) / tiles_total);
+  sw[2] = u_hi - u_lo + 1;
+  sw[0] = p.full_waves + sw[2];
+  sw[3] = base + u_lo;
+  sw[4] = (u_hi > u_lo && s % tiles_total != 0) ? 1 : 0;
+  sw[5] = static_cast<int>(s - static_cast<long long>(u_lo) * tiles_total);
+  sw[6] = static_cast<int>(e - static_cast<long long>(u_hi) * tiles_total);
+}
+
+// The k-th of this CTA's sw[0] work items.  In the balanced schedule the
+// whole units come first; among the pieces a leading one that starts inside
+// its unit runs last: in the fused ring its tiles lie in the ring blocks that
+// arrive last, while every other piece starts at block 0.
+__device__ __forceinline__ Item work_item(const FlashParams& p, int k, int tiles_total,
+                                          const int* sw) {
+  if (!p.balanced) return make_item(p, blockIdx.x + k * gridDim.x, tiles_total);
+  Item it;
+  if (k < sw[1]) {
+    set_unit(p, blockIdx.x + k * gridDim.x, it);
+    it.v_begin = 0;
+    it.v_end = tiles_total;
+    it.store = -1;
+    return it;
+  }
+  const int n = sw[2];
+  const int idx = (k - sw[1] + sw[4]) % n;
+  set_unit(p, sw[3] + idx, it);
+  it.v_begin = idx == 0 ? sw[5] : 0;
+  it.v_end = idx == n - 1 ? sw[6] : tiles_total;
+  const bool whole = it.v_begin == 0 && it.v_end == tiles_total;
+  it.store = whole ? -1 : 2 * static_cast<int>(blockIdx.x) + (idx == 0 ? 0 : 1);
   return it;
 }
 

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_copy_ok;
   __shared__ float s_xmax[2][2][kM];  // [tile parity][half][row] partial row maxima
   __shared__ float s_xl[2][2][kM];    // [item parity][half][row] partial row sums
+  __shared__ int s_work[kWorkWords];  // this CTA's work description (work_setup)
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -148,6 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_barrier_init();
   }
+  const int tpb = p.Skv / kN;                 // tiles per block
+  const int tiles_total = p.nblk * tpb;
+  if (threadIdx.x == 32) work_setup(p, tiles_total, s_work);
   if (warp == kWarpMma) {
     tmem_alloc(&tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -155,9 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-
-  const int tpb = p.Skv / kN;                 // tiles per block
-  const int tiles_total = p.nblk * tpb;
 
   if (warp == kWarpTma) {
     // ------------------------------------------------------------------ TMA
@@ -167,8 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       int ready_blocks = 1;  // blocks [0, ready_blocks) known present locally
       bool ok = true;
-      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-        const Item it = make_item(p, item, tiles_total);
+      const int n_work = s_work[0];
+      for (int w = 0; w < n_work && ok; ++w) {
+        const Item it = work_item(p, w, tiles_total, s_work);
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
           if (classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
@@ -233,8 +235,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int item_count = 0;
       int final_count = 0;  // items that had at least one visible tile
       bool ok = true;
-      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
-        const Item it = make_item(p, item, tiles_total);
+      const int n_work = s_work[0];
+      for (int w = 0; w < n_work && ok; ++w, ++item_count) {
+        const Item it = work_item(p, w, tiles_total, s_work);
         ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
         if (!ok) break;
         tc_fence_after();
@@ -349,8 +352,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int item_count = 0;
     int final_count = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
-      const Item it = make_item(p, item, tiles_total);
+    const int n_work = s_work[0];
+    for (int w = 0; w < n_work && ok; ++w, ++item_count) {
+      const Item it = work_item(p, w, tiles_total, s_work);
       const int qrow = it.q0 + row;
       // ---- this warpgroup's half of the Q row -> TMEM ----
       {
@@ -507,12 +511,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t o_tm = tmem + lane_base + C::kColO + half * kHalfD;
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
-      const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
-      const bool split = p.nsplit > 1;
+      // re-derived here (shared-memory reads) rather than kept live across the tile loop
+      const Item ie = work_item(p, w, tiles_total, s_work);
+      const size_t r = static_cast<size_t>(ie.q0 + row) * p.Hq + ie.h;
+      const bool split = ie.store >= 0;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
       float* dst_f32 = nullptr;
       if (split)
-        dst_f32 = p.split_acc + (static_cast<size_t>(item) * kM + row) * D + half * kHalfD;
+        dst_f32 = p.split_acc + (static_cast<size_t>(ie.store) * kM + row) * D + half * kHalfD;
       else if (p.partial)
         dst_f32 = p.acc + r * D + half * kHalfD;
       else if (!p.out_bf16)
@@ -551,8 +557,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (half == 0) {
         if (split) {
-          p.split_m[static_cast<size_t>(item) * kM + row] = m_nat;
-          p.split_l[static_cast<size_t>(item) * kM + row] = l_run;
+          p.split_m[static_cast<size_t>(ie.store) * kM + row] = m_nat;
+          p.split_l[static_cast<size_t>(ie.store) * kM + row] = l_run;
         } else if (p.partial) {
           if (p.m_out) p.m_out[r] = m_nat;
           if (p.l_out) p.l_out[r] = l_run;
@@ -573,38 +579,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// split merge: combine nsplit partials of each unit
+// split merge: combine the partial records of a unit
 // ---------------------------------------------------------------------------
+// Final (or partial-mode) write of merged row `row` of `unit`, column quad c.
 template <int D>
-__global__ void split_merge_kernel(const FlashParams p) {
-  constexpr int kTpr = D / 4;
-  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  const int R = p.rows_per_unit;
-  const long long rows_total = static_cast<long long>(p.n_units) * R;
-  const long long urow = t / kTpr;
-  const int c = static_cast<int>(t % kTpr);
-  if (urow >= rows_total) return;
-  const int unit = static_cast<int>(urow / R);
-  const int row = static_cast<int>(urow % R);
+__device__ __forceinline__ void write_merged(const FlashParams& p, int unit, int row, int c,
+                                             float mx, float l, float4 a) {
   const int h = unit_head(p, unit);
   const int qrow = unit_q0(p, unit) + row;
-  float mx = -INFINITY;
-  for (int k = 0; k < p.nsplit; ++k)
-    mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * R + row]);
-  const float mref = (mx == -INFINITY) ? 0.f : mx;
-  float l = 0.f;
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k = 0; k < p.nsplit; ++k) {
-    const size_t it = static_cast<size_t>(k) * p.n_units + unit;
-    const float mk = p.split_m[it * R + row];
-    const float w = (mk == -INFINITY) ? 0.f : expf(mk - mref);
-    l += w * p.split_l[it * R + row];
-    const float4 x = reinterpret_cast<const float4*>(p.split_acc + (it * R + row) * D)[c];
-    a.x += w * x.x;
-    a.y += w * x.y;
-    a.z += w * x.z;
-    a.w += w * x.w;
-  }
   const size_t r = static_cast<size_t>(qrow) * p.Hq + h;
   if (p.partial) {
     reinterpret_cast<float4*>(p.acc + r * D)[c] = a;
@@ -628,6 +610,86 @@ __global__ void split_merge_kernel(const FlashParams p) {
     reinterpret_cast<float4*>(static_cast<float*>(p.out) + r * D)[c] = a;
   }
   if (c == 0 && p.lse != nullptr) p.lse[r] = l > 0.f ? mx + logf(l) : -INFINITY;
+}
+
+// Accumulate record `rec` of R rows (row `row`, column quad c) into the running
+// merge relative to the reference max `mref`.
+template <int D>
+__device__ __forceinline__ void add_record(const FlashParams& p, size_t rec, int R, int row, int c,
+                                           float mref, float& l, float4& a) {
+  const float mk = p.split_m[rec * R + row];
+  const float w = (mk == -INFINITY) ? 0.f : expf(mk - mref);
+  l += w * p.split_l[rec * R + row];
+  const float4 x = reinterpret_cast<const float4*>(p.split_acc + (rec * R + row) * D)[c];
+  a.x += w * x.x;
+  a.y += w * x.y;
+  a.z += w * x.z;
+  a.w += w * x.w;
+}
+
+// Equal-split schedule: unit u has records k * n_units + u, k < nsplit.
+template <int D>
+__global__ void split_merge_kernel(const FlashParams p) {
+  constexpr int kTpr = D / 4;
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const int R = p.rows_per_unit;
+  const long long rows_total = static_cast<long long>(p.n_units) * R;
+  const long long urow = t / kTpr;
+  const int c = static_cast<int>(t % kTpr);
+  if (urow >= rows_total) return;
+  const int unit = static_cast<int>(urow / R);
+  const int row = static_cast<int>(urow % R);
+  float mx = -INFINITY;
+  for (int k = 0; k < p.nsplit; ++k)
+    mx = fmaxf(mx, p.split_m[(static_cast<size_t>(k) * p.n_units + unit) * R + row]);
+  const float mref = (mx == -INFINITY) ? 0.f : mx;
+  float l = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < p.nsplit; ++k)
+    add_record<D>(p, static_cast<size_t>(k) * p.n_units + unit, R, row, c, mref, l, a);
+  write_merged<D>(p, unit, row, c, mx, l, a);
+}
+
+// Balanced schedule: blockIdx.y + 1 = b indexes the boundary between CTAs b-1
+// and b in the shared-out remainder.  A boundary strictly inside unit u, and
+// the first such boundary of u, merges u from the records of CTAs b-1, b, ...
+// whose ranges meet u (record 2c when u holds the first tile of CTA c's
+// range, else 2c + 1).
+template <int D>
+__global__ void balanced_merge_kernel(const FlashParams p) {
+  constexpr int kTpr = D / 4;
+  const int G = p.n_items;
+  const int b = blockIdx.y + 1;
+  const long long tt = p.kv_tiles;
+  const int base = p.full_waves * G;
+  const long long T = static_cast<long long>(p.n_units - base) * tt;
+  const long long bt = balanced_start(T, G, b);
+  const int urel = static_cast<int>(bt / tt);
+  const long long u0 = urel * tt;
+  const int unit = base + urel;
+  if (bt == u0 || balanced_start(T, G, b - 1) > u0) return;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = t / kTpr;
+  const int c = t % kTpr;
+  if (row >= kM) return;
+  float mx = -INFINITY;
+  for (int cta = b - 1; cta < G; ++cta) {
+    const long long s = balanced_start(T, G, cta);
+    if (s >= u0 + tt) break;
+    if (balanced_start(T, G, cta + 1) <= s) continue;  // empty range
+    const size_t rec = 2 * static_cast<size_t>(cta) + (s >= u0 ? 0 : 1);
+    mx = fmaxf(mx, p.split_m[rec * kM + row]);
+  }
+  const float mref = (mx == -INFINITY) ? 0.f : mx;
+  float l = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int cta = b - 1; cta < G; ++cta) {
+    const long long s = balanced_start(T, G, cta);
+    if (s >= u0 + tt) break;
+    if (balanced_start(T, G, cta + 1) <= s) continue;
+    add_record<D>(p, 2 * static_cast<size_t>(cta) + (s >= u0 ? 0 : 1), kM, row, c, mref, l, a);
+  }
+  write_merged<D>(p, unit, row, c, mx, l, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -782,11 +844,35 @@ int flash_choose_split(int units, int tiles_per_unit, int sms, int overhead_tile
   return best;
 }
 
+bool flash_prefer_balanced(int units, int tiles_per_unit, int sms, int overhead_tiles) {
+  // Balanced: floor(units / G) whole-unit waves, then the remainder's
+  // ceil(R * tiles / G) tiles per CTA in at most two pieces, plus the merge
+  // pass (about four tiles of either kernel on B200).  It has to beat the best
+  // equal split by 2 % to be worth the partial records.
+  const long long full = units / sms;
+  const long long R = units - full * sms;
+  if (R == 0) return false;
+  const long long per = (R * tiles_per_unit + sms - 1) / sms;
+  const long long pieces = (per + tiles_per_unit - 1) / tiles_per_unit + 1;
+  const double bal = static_cast<double>(full * (tiles_per_unit + overhead_tiles) + per +
+                                         pieces * overhead_tiles + 4);
+  const int c = flash_choose_split(units, tiles_per_unit, sms, overhead_tiles);
+  const long long items = static_cast<long long>(units) * c;
+  const double split = static_cast<double>((items + sms - 1) / sms) *
+                       (static_cast<double>(tiles_per_unit) / c + overhead_tiles);
+  return bal < 0.98 * split;
+}
+
 int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps, int grid,
                          bool cooperative, cudaStream_t stream) {
   if (p.Sq % kM != 0) throw std::runtime_error("flash: query rows must be a multiple of 128");
   if (p.Hq % p.Hkv != 0) throw std::runtime_error("flash: Hq must be a multiple of Hkv");
   if (p.nblk > kMaxSlots) throw std::runtime_error("flash: too many blocks");
+  if (p.balanced && (grid != p.n_items || p.causal || p.rows_per_unit != kM ||
+                     p.full_waves < 0 || p.full_waves * grid > p.n_units))
+    throw std::runtime_error(
+        "flash: balanced schedule needs grid == n_items, full_waves * grid <= units and no "
+        "causal mask");
   if (p.causal && p.zigzag && (p.Sq != p.Skv || (p.Sq / 2) % kM != 0))
     throw std::runtime_error("flash: zigzag causal needs Sq == Skv and Sq/2 a multiple of 128");
   if (prec == Prec::kF32x3) {
@@ -799,6 +885,16 @@ int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps,
 }
 
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream) {
+  if (p.balanced) {
+    if (p.n_items < 2) return 0;
+    const int bs = 256;
+    const dim3 grid((kM * (p.D / 4) + bs - 1) / bs, p.n_items - 1);
+    if (p.D == 64)
+      balanced_merge_kernel<64><<<grid, bs, 0, stream>>>(p);
+    else
+      balanced_merge_kernel<128><<<grid, bs, 0, stream>>>(p);
+    return static_cast<int>(cudaGetLastError());
+  }
   const long long threads_total = static_cast<long long>(p.n_units) * p.rows_per_unit * (p.D / 4);
   const int bs = 256;
   const int blocks = static_cast<int>((threads_total + bs - 1) / bs);

@@ -39,20 +39,38 @@ bool two_tile_enabled() {
   return e != nullptr && std::strcmp(e, "1") == 0;
 }
 
+int tiles_of(const FlashArgs& a) { return a.nblk * (a.Skv / (a.prec == Prec::kF32x3 ? 64 : 128)); }
+
 }  // namespace
 
 FlashPlan flash_plan(const FlashArgs& a) {
   if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
-  FlashPlan pl;
-  const int kN = a.prec == Prec::kF32x3 ? 64 : 128;
+  FlashPlan pl{};
   // bf16 may use the two-query-tile kernel when the rows split into 256-row units
   pl.rows_per_unit = (a.prec == Prec::kBF16 && a.Sq % 256 == 0 && two_tile_enabled()) ? 256 : 128;
   pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
-  const int tiles = a.nblk * (a.Skv / kN);
+  const int tiles = tiles_of(a);
   const int sms = flash_sm_count();
   // per-item overhead in tiles: ~6 of the fp32 kernel's 64-key tiles, ~3 of 128-key bf16 tiles
-  pl.nsplit = a.nsplit > 0 ? a.nsplit
-                           : flash_choose_split(pl.n_units, tiles, sms, a.prec == Prec::kF32x3 ? 6 : 3);
+  const int overhead = a.prec == Prec::kF32x3 ? 6 : 3;
+  // the balanced schedule needs equal-cost tiles (no causal mask) and 128-row units
+  const bool can_balance = !a.causal && pl.rows_per_unit == 128;
+  if (a.nsplit < 0 && !can_balance)
+    throw std::runtime_error("flash: the balanced schedule needs causal=0 and 128-row units");
+  pl.balanced = (a.nsplit < 0 ||
+                 (a.nsplit == 0 && can_balance &&
+                  flash_prefer_balanced(pl.n_units, tiles, sms, overhead)))
+                    ? 1
+                    : 0;
+  if (pl.balanced) {
+    pl.nsplit = 1;
+    pl.grid = a.grid > 0 ? a.grid : sms;
+    pl.n_items = pl.grid;  // one balanced range per CTA
+    pl.full_waves = pl.n_units / pl.grid;
+    pl.workspace_bytes = static_cast<size_t>(2 * pl.grid) * 128 * (a.D + 2) * sizeof(float);
+    return pl;
+  }
+  pl.nsplit = a.nsplit > 0 ? a.nsplit : flash_choose_split(pl.n_units, tiles, sms, overhead);
   if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;
   pl.n_items = pl.n_units * pl.nsplit;
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
@@ -64,7 +82,8 @@ FlashPlan flash_plan(const FlashArgs& a) {
 }
 
 int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
-  if (pl.nsplit > 1 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace_bytes))
+  const bool records = pl.nsplit > 1 || pl.balanced;
+  if (records && (a.workspace == nullptr || a.workspace_bytes < pl.workspace_bytes))
     throw std::runtime_error("flash: split workspace missing or too small");
   FlashParams p;
   std::memset(&p, 0, sizeof(p));
@@ -82,6 +101,9 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.rank = a.rank;
   p.blk_offset = a.blk_offset;
   p.nsplit = pl.nsplit;
+  p.balanced = pl.balanced;
+  p.full_waves = pl.balanced ? pl.full_waves : 0;
+  p.kv_tiles = tiles_of(a);
   p.rows_per_unit = pl.rows_per_unit;
   p.n_units = pl.n_units;
   p.n_items = pl.n_items;
@@ -92,11 +114,14 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.acc = a.acc;
   p.m_out = a.m;
   p.l_out = a.l;
-  if (pl.nsplit > 1) {
+  if (records) {
+    // nsplit > 1: one record per item; balanced: two per CTA (n_items == CTAs)
+    const size_t rec_rows =
+        static_cast<size_t>(pl.balanced ? 2 * pl.n_items : pl.n_items) * pl.rows_per_unit;
     float* ws = static_cast<float*>(a.workspace);
     p.split_acc = ws;
-    p.split_m = ws + static_cast<size_t>(pl.n_items) * pl.rows_per_unit * a.D;
-    p.split_l = p.split_m + static_cast<size_t>(pl.n_items) * pl.rows_per_unit;
+    p.split_m = ws + rec_rows * a.D;
+    p.split_l = p.split_m + rec_rows;
   }
   p.fused = a.fused ? 1 : 0;
   p.ring_chain = a.ring_chain ? 1 : 0;
@@ -123,7 +148,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
     err = flash_forward_launch(a.prec, p, maps, pl.grid, a.fused, stream);
   }
   if (err != 0) return err;
-  if (pl.nsplit > 1) err = flash_split_merge_launch(p, stream);
+  if (records) err = flash_split_merge_launch(p, stream);
   return err;
 }
 

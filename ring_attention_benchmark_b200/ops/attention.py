@@ -91,6 +91,11 @@ def flash_attention(
     With ``causal`` the mask uses global positions: block i comes from rank
     ``(rank - i) % world``; ``zigzag`` selects the balanced sharding in which
     rank r holds global chunks r and 2*world-1-r.
+
+    ``nsplit`` picks the work schedule of the persistent kernel: 0 lets the
+    planner choose, n > 0 splits every 128-row query tile's KV range into n
+    equal chunks, -1 forces the balanced schedule (each CTA takes an equal
+    share of all (query tile, KV tile) pairs; needs ``causal=False``).
     """
     C = load()
     prec = prec_of(q.dtype)
@@ -117,8 +122,12 @@ def partial_attention(
     scale: float = 1.0,
     kernel: str = "tcgen05",
     out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+    nsplit: int = 0,
 ):
-    """One ring step: returns (acc unnormalised, m natural-log row max, l row sum)."""
+    """One ring step: returns (acc unnormalised, m natural-log row max, l row sum).
+
+    ``nsplit`` selects the work schedule as in :func:`flash_attention`.
+    """
     C = load()
     sq, hq, d = q.shape
     if out is None:
@@ -136,7 +145,7 @@ def partial_attention(
     slots = ring_slots([k], [v])
     status = new_status(q.device)
     C.flash_fwd(prec, q.contiguous(), slots, 1, k.shape[0], k.shape[1], scale=scale, acc=acc,
-                m=m, l=l, status=status)
+                m=m, l=l, status=status, nsplit=nsplit)
     check_status(status, "flash_fwd(partial)")
     return acc, m, l
 

@@ -76,6 +76,44 @@ def test_ring_blocks_gqa(cuda_device, dtype, d, nsplit):
         assert (out.double() - ref).abs().max().item() < tol
 
 
+@pytest.mark.parametrize("dtype,d,spr,heads,world", [
+    (torch.float32, 64, 2048, 1, 3),     # 16 query tiles on every SM: many CTAs per tile
+    (torch.bfloat16, 128, 4096, 8, 1),   # 256 query tiles: whole tiles plus cut ones per CTA
+    (torch.bfloat16, 64, 384, 3, 2),     # fewer (tile, KV tile) pairs than CTAs: empty ranges
+    (torch.bfloat16, 64, 512, 37, 1),    # 148 query tiles: one whole wave on a 148-SM B200
+])
+def test_balanced_schedule(cuda_device, dtype, d, spr, heads, world):
+    """Balanced schedule (nsplit=-1): whole waves of query tiles, then equal
+    (query tile, KV tile) shares of the rest per CTA, cut query tiles merged
+    from the CTAs' partial records."""
+    qs, ks, vs = _blocks(world, spr, heads, 1, d, dtype, seed=6)
+    for rank in range(world):
+        out, lse = _run_rank(cuda_device, qs, ks, vs, rank, world, nsplit=-1)
+        ref, rlse = _oracle_rank(qs, ks, vs, rank, world)
+        tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
+        assert (out.double() - ref).abs().max().item() < tol
+        assert (lse.double() - rlse).abs().max().item() < tol
+
+
+def test_balanced_schedule_partial_contract(cuda_device):
+    x = inputs.normal_inputs(0, 1024, 2, 64)
+    y = inputs.normal_inputs(1, 1024, 2, 64)
+    dev = cuda_device
+    acc, m, l = A.partial_attention(x.q.to(dev), y.k.to(dev), y.v.to(dev), x.scale, nsplit=-1)
+    torch.cuda.synchronize()
+    racc, rm, rl = oracle.partial_attention(x.q, y.k, y.v, x.scale)
+    out = acc.cpu().double() / l.cpu().double().unsqueeze(-1)
+    assert torch.allclose(out, racc / rl.unsqueeze(-1), atol=2e-5)
+    assert torch.allclose(m.cpu().double() + torch.log(l.cpu().double()), rm + torch.log(rl),
+                          atol=2e-5)
+
+
+def test_balanced_schedule_rejects_causal(cuda_device):
+    qs, ks, vs = _blocks(1, 256, 1, 1, 64, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="balanced"):
+        _run_rank(cuda_device, qs, ks, vs, 0, 1, causal=True, nsplit=-1)
+
+
 @pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float32, 64)])
 def test_zigzag_causal(cuda_device, dtype, d):
     world = 2
