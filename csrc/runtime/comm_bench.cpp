@@ -107,7 +107,7 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   cuda_check(cudaEventCreate(&ev0), "event");
   cuda_check(cudaEventCreate(&ev1), "event");
   cuda_check(cudaEventCreate(&done), "event");
-  const int slices = o.slices > 0 ? std::min(o.slices, static_cast<int>(kMaxSlices)) : 64;
+  const int slices = o.slices > 0 ? std::min(o.slices, static_cast<int>(kMaxSlices)) : 148;
 
   RingCopyParams rp;
   std::memset(&rp, 0, sizeof(rp));
@@ -243,6 +243,33 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   cudaEventDestroy(ev0);
   cudaEventDestroy(ev1);
   cudaEventDestroy(done);
+  // Full-content check of the last repetition (the precheck, like the
+  // reference's, looks at one float per step): after np-1 steps this rank
+  // holds the whole shard of rank (rank + 1) mod np.  Every rank takes part in
+  // the reduction, so all of them fail together.
+  if (o.precheck && np > 1 && o.warmup + o.iters > 0) {
+    std::vector<float> got(n_floats);
+    cuda_check(cudaMemcpy(got.data(), (np - 1) & 1 ? d2 : d1, o.bytes, cudaMemcpyDeviceToHost),
+                          "D2H final check");
+    const int src = (rank + 1) % np;
+    size_t bad = n_floats;
+    for (size_t i = 0; i < n_floats; ++i)
+      if (got[i] != src * 1000.0f + static_cast<float>(i)) {
+        bad = i;
+        break;
+      }
+    const double any_bad = ctx.host().reduce_max({bad < n_floats ? 1.0 : 0.0})[0];
+    if (any_bad > 0.0) {
+      res.precheck_ok = false;
+      res.precheck_msg =
+          bad < n_floats
+              ? strfmt("rank %d: final buffer differs at float %zu: got %g, expected %g", rank,
+                       bad, static_cast<double>(got[bad]),
+                       static_cast<double>(src * 1000.0f + static_cast<float>(bad)))
+              : strfmt("rank %d: another rank's final buffer is wrong", rank);
+      throw RankFailure("final content check failed: " + res.precheck_msg);
+    }
+  }
   const double n = o.iters > 0 ? o.iters : 1;
   res.avg_ms["d2h"] = sum[0] / n;
   res.avg_ms["mpi"] = sum[1] / n;
