@@ -135,9 +135,14 @@ __device__ __forceinline__ int global_pos(int local, int owner, int S, int W, in
 
 // Tile classification for the 128-row query tile starting at local row q0:
 // 0 = skip (fully masked), 1 = full, 2 = diagonal (mask per element).
-__device__ __forceinline__ int classify(const FlashParams& p, int q0, int v, int kN, int tpb,
+// On 0, *v_io moves to the last tile of v's key chunk: keys grow along each
+// contiguous chunk of a ring block (the whole block, or each half under
+// zigzag sharding), so every later tile of the chunk is masked as well and a
+// loop over v continues after it.
+__device__ __forceinline__ int classify(const FlashParams& p, int q0, int* v_io, int kN, int tpb,
                                         int* k_lo_out, int* q_lo_out) {
   if (!p.causal) return 1;
+  const int v = *v_io;
   const int s = v / tpb, t = v - (v / tpb) * tpb;
   const int owner = ((p.rank - p.blk_offset - s) % p.world + p.world) % p.world;
   const int q_lo = global_pos(q0, p.rank, p.Sq, p.world, p.zigzag);
@@ -146,7 +151,11 @@ __device__ __forceinline__ int classify(const FlashParams& p, int q0, int v, int
   const int k_hi = k_lo + kN - 1;
   *k_lo_out = k_lo;
   *q_lo_out = q_lo;
-  if (k_lo > q_hi) return 0;
+  if (k_lo > q_hi) {
+    const int chunk = p.zigzag ? tpb / 2 : tpb;
+    *v_io = s * tpb + (t / chunk + 1) * chunk - 1;
+    return 0;
+  }
   if (k_hi <= q_lo) return 1;
   return 2;
 }

@@ -65,10 +65,13 @@ __device__ __forceinline__ uint32_t col_s(int x) { return x ? 128u : 0u; }
 __device__ __forceinline__ uint32_t col_o(int x) { return x ? 384u : 256u; }
 
 // A KV tile is processed when it is visible to either query tile of the unit.
-__device__ __forceinline__ bool visible2(const FlashParams& p, int q0, int v, int tpb) {
+// When it is not, *v_io moves to the end of the masked run (masked for the
+// second, later query tile means masked for both).
+__device__ __forceinline__ bool visible2(const FlashParams& p, int q0, int* v_io, int tpb) {
   int a, b;
-  return classify(p, q0, v, 128, tpb, &a, &b) != 0 ||
-         classify(p, q0 + kM, v, 128, tpb, &a, &b) != 0;
+  int v1 = *v_io;
+  if (classify(p, q0, &v1, 128, tpb, &a, &b) != 0) return true;
+  return classify(p, q0 + kM, v_io, 128, tpb, &a, &b) != 0;
 }
 
 template <int D>
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
             tma_load_3d(sQ + x * C::kQTile + ds * (kM * 128), &tmQ, q_full, ds * 64, it.h,
                         it.q0 + x * kM);
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if (!visible2(p, it.q0, v, tpb)) continue;
+          if (!visible2(p, it.q0, &v, tpb)) continue;
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tc_fence_after();
         int j = 0;
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if (!visible2(p, it.q0, v, tpb)) continue;
+          if (!visible2(p, it.q0, &v, tpb)) continue;
           const int stage = g % NS;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
           if (!ok) break;
@@ -276,9 +279,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-        if (!visible2(p, it.q0, v, tpb)) continue;
+        if (!visible2(p, it.q0, &v, tpb)) continue;
         int k_lo = 0, q_lo = 0;
-        const int cls = classify(p, q0, v, kN, tpb, &k_lo, &q_lo);
+        int vq = v;  // this query tile's own classification; v itself is visible to the unit
+        const int cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
         const int lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);  // visible cols <= lim
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], g & 1, st, kSiteSFull, tmo));
         if (!ok) break;

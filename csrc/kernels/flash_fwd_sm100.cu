@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Item it = work_item(p, w, tiles_total, s_work);
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
-          if (classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
-          if (classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
           const int stage = g % NS;
           const int b = g & 1;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
@@ -401,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
         int k_lo = 0, q_lo = 0;
-        const int cls = classify(p, it.q0, v, kN, tpb, &k_lo, &q_lo);
-        if (cls == 0) continue;
+        const int cls = classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo);
+        if (cls == 0) continue;  // v moved to the end of the masked run
         const int b = g & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo));
         if (!ok) break;
@@ -458,8 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
         if constexpr (C::kTF32) {
+          float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
           uint32_t pb[32], psm[32];
 #pragma unroll
           for (int c = 0; c < kHalfN; c += 32) {
@@ -472,7 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(s_tm + half * kHalfN + c, pb);
             tmem_st32(tmem + lane_base + (b ? C::kColPs1 : C::kColPs0) + half * kHalfN + c, psm);
           }
+          l_part += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
         } else {
+          // four partial sums: the bf16 d=128 instance sits at the 168-register cap
+          float ps4[4] = {0.f, 0.f, 0.f, 0.f};
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < kHalfN; c += 64) {
@@ -480,13 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i]), sl2, -m_use));
               const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c + 2 * i + 1]), sl2, -m_use));
-              ps8[i & 7] += e0 + e1;
+              ps4[i & 3] += e0 + e1;
               pk[i] = pack_bf16x2(e0, e1);
             }
             tmem_st32(s_tm + (half * kHalfN + c) / 2, pk);
           }
+          l_part += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
         }
-        l_part += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[b]);
