@@ -48,6 +48,7 @@ struct FlashParams {
                         //    remaining units' (unit, KV tile) space shared out evenly, CTA c
                         //    owning tiles [c*T/G, (c+1)*T/G); needs causal == 0, 128-row units
   int full_waves;       // balanced: whole-unit waves before the shared-out remainder
+  int dynamic;          // 1: CTAs claim equal-split items from a counter in the status block
   int kv_tiles;         // KV tiles of one unit over the whole ring (nblk * Skv / tile keys)
   int rows_per_unit;    // query rows of one work unit (128, or 256 for the two-tile bf16 kernel)
   int n_units;          // heads * Sq / rows_per_unit
@@ -171,6 +172,7 @@ struct FlashPlan {
   int nsplit;         // equal-split chunks per unit; 1 under the balanced schedule
   int balanced;       // 1: balanced schedule (n_items == grid == CTAs)
   int full_waves;     // balanced: whole-unit waves before the shared-out remainder
+  int dynamic;        // 1: dynamic claiming of equal-split items (causal, one-tile kernel)
   int n_units;
   int n_items;
   int grid;

@@ -36,6 +36,7 @@ enum WaitSite : uint32_t {
   kSiteRingFlag = 13,      // comm-only ring copy flag
   kSiteTest = 14,          // deliberately unsatisfiable wait used by tests
   kSitePvDone = 15,
+  kSiteItemQueue = 16,     // flash kernel's in-CTA work-item queue
 };
 
 struct DeviceStatus {
@@ -44,6 +45,9 @@ struct DeviceStatus {
   uint32_t block;      // blockIdx.x that recorded it
   uint32_t detail;     // site-specific (step, tile, peer...)
   uint32_t n_errors;   // how many threads/blocks hit an error
+  // [0] work-item claim counter and [1] finished-CTA counter of the flash
+  // kernel's dynamic schedule; zero between launches (the last CTA resets
+  // them), so one status block serves one launch at a time.
   uint32_t pad[3];
 };
 

@@ -102,6 +102,10 @@ __device__ __forceinline__ void work_setup(const FlashParams& p, int tiles_total
   sw[6] = static_cast<int>(e - static_cast<long long>(u_hi) * tiles_total);
 }
 
+// Depth of the shared-memory queue through which the TMA thread hands work
+// items to the MMA and softmax roles.
+constexpr int kItemSlots = 4;
+
 // The k-th of this CTA's sw[0] work items.  In the balanced schedule the
 // whole units come first; among the pieces a leading one that starts inside
 // its unit runs last: in the fused ring its tiles lie in the ring blocks that
@@ -125,6 +129,25 @@ __device__ __forceinline__ Item work_item(const FlashParams& p, int k, int tiles
   const bool whole = it.v_begin == 0 && it.v_end == tiles_total;
   it.store = whole ? -1 : 2 * static_cast<int>(blockIdx.x) + (idx == 0 ? 0 : 1);
   return it;
+}
+
+// Work item w of this CTA, false when the CTA has no more.  The static
+// schedules take the w-th entry of the CTA's precomputed list; the dynamic one
+// (p.dynamic) claims the next unclaimed item of the whole grid from a counter
+// in the status block (pad[0]), so a CTA that drew cheap items (short causal
+// query tiles) takes more of them.  Items are claimed in order, so the cheap
+// tail of the longest-first order balances the end of the schedule.
+__device__ __forceinline__ bool next_item(const FlashParams& p, int w, int tiles_total,
+                                          const int* sw, Item* it) {
+  if (p.dynamic) {
+    const uint32_t i = atomicAdd(&p.status->pad[0], 1u);
+    if (i >= static_cast<uint32_t>(p.n_items)) return false;
+    *it = make_item(p, static_cast<int>(i), tiles_total);
+    return true;
+  }
+  if (w >= sw[0]) return false;
+  *it = work_item(p, w, tiles_total, sw);
+  return true;
 }
 
 __device__ __forceinline__ int global_pos(int local, int owner, int S, int W, int zigzag) {

@@ -72,7 +72,7 @@ struct Cfg {
   static constexpr int kVTile = kKTile;
   static constexpr int kStages = (kKTile + kVTile) <= 32768 ? 4 : 3;
   static constexpr int kSmemTiles = kStages * (kKTile + kVTile);
-  static constexpr int kNumBars = 4 * kStages + 12;
+  static constexpr int kNumBars = 4 * kStages + 12 + 2 * kItemSlots;
   static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
   // TMEM columns
   static constexpr uint32_t kColQ = 0;                       // Q (tf32: Qb at 0, Qs at D)
@@ -117,11 +117,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 4 * NS + 7;
   uint64_t* xbar = bars + 4 * NS + 8;   // [2] row-max exchange between the softmax halves
   uint64_t* lbar = bars + 4 * NS + 10;  // [2] row-sum exchange
+  uint64_t* item_full = bars + 4 * NS + 12;                 // [kItemSlots] work-item queue
+  uint64_t* item_empty = bars + 4 * NS + 12 + kItemSlots;  // [kItemSlots]
   __shared__ uint32_t tmem_slot;
   __shared__ int s_copy_ok;
   __shared__ float s_xmax[2][2][kM];  // [tile parity][half][row] partial row maxima
   __shared__ float s_xl[2][2][kM];    // [item parity][half][row] partial row sums
   __shared__ int s_work[kWorkWords];  // this CTA's work description (work_setup)
+  __shared__ Item s_items[kItemSlots];  // work-item queue: TMA thread -> MMA and softmax roles
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -147,6 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&xbar[i], 256);
       mbar_init(&lbar[i], 256);
     }
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 1 + 8);  // the MMA thread + one lane per softmax warp
+    }
     fence_barrier_init();
   }
   const int tpb = p.Skv / kN;                 // tiles per block
@@ -168,9 +175,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       int ready_blocks = 1;  // blocks [0, ready_blocks) known present locally
       bool ok = true;
-      const int n_work = s_work[0];
-      for (int w = 0; w < n_work && ok; ++w) {
-        const Item it = work_item(p, w, tiles_total, s_work);
+      for (int w = 0; ok; ++w) {
+        // publish work item w (or the end marker) to the MMA and softmax roles
+        const int slot = w % kItemSlots;
+        if (w >= kItemSlots) {
+          ok = mbar_wait(&item_empty[slot], ((w / kItemSlots) - 1) & 1, st, kSiteItemQueue, tmo);
+          if (!ok) break;
+        }
+        Item it;
+        const bool have = next_item(p, w, tiles_total, s_work, &it);
+        if (!have) it.unit = -1;
+        s_items[slot] = it;
+        mbar_arrive(&item_full[slot]);
+        if (!have) break;
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
           if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
@@ -235,9 +252,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int item_count = 0;
       int final_count = 0;  // items that had at least one visible tile
       bool ok = true;
-      const int n_work = s_work[0];
-      for (int w = 0; w < n_work && ok; ++w, ++item_count) {
-        const Item it = work_item(p, w, tiles_total, s_work);
+      for (int w = 0; ok; ++w, ++item_count) {
+        const int slot = w % kItemSlots;
+        ok = mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st, kSiteItemQueue, tmo);
+        if (!ok) break;
+        const Item it = s_items[slot];
+        mbar_arrive(&item_empty[slot]);  // the item now lives in registers
+        if (it.unit < 0) break;
         ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
         if (!ok) break;
         tc_fence_after();
@@ -352,9 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int item_count = 0;
     int final_count = 0;
     bool ok = true;
-    const int n_work = s_work[0];
-    for (int w = 0; w < n_work && ok; ++w, ++item_count) {
-      const Item it = work_item(p, w, tiles_total, s_work);
+    for (int w = 0; ok; ++w, ++item_count) {
+      const int slot = w % kItemSlots;
+      ok = __all_sync(0xffffffffu, mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st,
+                                             kSiteItemQueue, tmo));
+      if (!ok) break;
+      const Item it = s_items[slot];
+      if (it.unit < 0) break;
       const int qrow = it.q0 + row;
       // ---- this warpgroup's half of the Q row -> TMEM ----
       {
@@ -514,8 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t o_tm = tmem + lane_base + C::kColO + half * kHalfD;
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
-      // re-derived here (shared-memory reads) rather than kept live across the tile loop
-      const Item ie = work_item(p, w, tiles_total, s_work);
+      // re-read here from the queue slot rather than kept live across the tile loop
+      const Item ie = s_items[slot];
       const size_t r = static_cast<size_t>(ie.q0 + row) * p.Hq + ie.h;
       const bool split = ie.store >= 0;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
@@ -571,10 +596,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // all TMEM reads of this item are done before the next Q lands in TMEM
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[slot]);  // queue slot free again
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (p.dynamic && threadIdx.x == 0) {
+    // Every CTA has stopped claiming items once it gets here; the last one
+    // resets the claim counter for the next launch that uses this status block.
+    __threadfence();
+    if (atomicAdd(&st->pad[1], 1u) == gridDim.x - 1) {
+      atomicExch(&st->pad[0], 0u);
+      atomicExch(&st->pad[1], 0u);
+    }
+  }
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

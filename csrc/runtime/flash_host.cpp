@@ -34,6 +34,13 @@ const FlashMaps& cached_maps(Prec prec, const void* k, const void* v, size_t str
 // The two-query-tile bf16 kernel is opt-in (RAB_FLASH_2Q=1): measured on B200
 // it trails the one-tile kernel, whose head-major work order already keeps
 // the tensor and exp pipes equally busy.
+// Dynamic claiming of work items (causal one-tile launches) is on unless
+// RAB_FLASH_DYNAMIC=0.
+bool dynamic_enabled() {
+  const char* e = std::getenv("RAB_FLASH_DYNAMIC");
+  return e == nullptr || std::strcmp(e, "0") != 0;
+}
+
 bool two_tile_enabled() {
   const char* e = std::getenv("RAB_FLASH_2Q");
   return e != nullptr && std::strcmp(e, "1") == 0;
@@ -78,6 +85,9 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.workspace_bytes = pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * pl.rows_per_unit *
                                            (a.D + 2) * sizeof(float)
                                      : 0;
+  // causal items differ in cost: claim them dynamically (the two-tile kernel keeps its
+  // static order)
+  pl.dynamic = (a.causal && pl.rows_per_unit == 128 && dynamic_enabled()) ? 1 : 0;
   return pl;
 }
 
@@ -103,6 +113,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.nsplit = pl.nsplit;
   p.balanced = pl.balanced;
   p.full_waves = pl.balanced ? pl.full_waves : 0;
+  p.dynamic = pl.dynamic;
   p.kv_tiles = tiles_of(a);
   p.rows_per_unit = pl.rows_per_unit;
   p.n_units = pl.n_units;

@@ -44,7 +44,7 @@ class DeviceTimeout(RuntimeError):
 WAIT_SITES = {
     1: "q_full", 2: "k_full", 3: "v_full", 4: "k_empty", 5: "v_empty", 6: "s_full",
     7: "p_full", 8: "o_ready", 9: "block_ready", 10: "peer_ready", 11: "peer_consumed",
-    12: "copy_slice", 13: "ring_flag", 14: "test", 15: "pv_done",
+    12: "copy_slice", 13: "ring_flag", 14: "test", 15: "pv_done", 16: "item_queue",
 }
 
 

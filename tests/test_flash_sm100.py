@@ -115,6 +115,32 @@ def test_balanced_schedule_rejects_causal(cuda_device):
 
 
 @pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float32, 64)])
+def test_dynamic_schedule_reuses_status(cuda_device, dtype, d):
+    """Causal launches claim work items from a counter in the status block; the
+    last CTA resets it, so back-to-back launches on one status block stay exact
+    and leave the counter words at zero."""
+    C = A.load()
+    world = 2
+    qs, ks, vs = _blocks(world, 1024, 3, 1, d, dtype, seed=7)
+    dev = cuda_device
+    status = A.new_status(dev)
+    for rank in range(world):
+        order = oracle.ring_block_order(rank, world)
+        slots = A.ring_slots([ks[s].to(dev) for s in order], [vs[s].to(dev) for s in order])
+        q = qs[rank].to(dev)
+        ref, _ = _oracle_rank(qs, ks, vs, rank, world, causal=True, zigzag=True)
+        for _ in range(3):
+            out = torch.empty_like(q)
+            C.flash_fwd(A.prec_of(dtype), q, slots, world, 1024, 1, out=out, scale=d ** -0.5,
+                        causal=True, zigzag=True, world=world, rank=rank, status=status)
+            torch.cuda.synchronize()
+            A.check_status(status)
+            assert status.tolist()[5:7] == [0, 0]
+            tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
+            assert (out.float().cpu().double() - ref).abs().max().item() < tol
+
+
+@pytest.mark.parametrize("dtype,d", [(torch.bfloat16, 128), (torch.float32, 64)])
 def test_zigzag_causal(cuda_device, dtype, d):
     world = 2
     qs, ks, vs = _blocks(world, 512, 2, 1, d, dtype, seed=3)
