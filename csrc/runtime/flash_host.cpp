@@ -6,8 +6,11 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <queue>
 #include <stdexcept>
 #include <tuple>
+#include <utility>
+#include <vector>
 
 #include "flash.h"
 
@@ -46,6 +49,86 @@ bool two_tile_enabled() {
   return e != nullptr && std::strcmp(e, "1") == 0;
 }
 
+// Visible KV tiles of the 128-row query tile at local row q0, as ranges of
+// ring tile indices: keys grow along each contiguous chunk of a ring block
+// (the whole block, or each half under zigzag), so each chunk contributes the
+// run of tiles from its start up to the last one whose first key is <= the
+// tile's last query position (the same rule as the kernel's classify()).
+std::vector<std::pair<int, int>> visible_ranges(const FlashArgs& a, int kN, int q0) {
+  auto gpos = [&](int local, int owner, int S) -> long long {
+    if (!a.zigzag) return static_cast<long long>(owner) * S + local;
+    const int Ch = S / 2;
+    return local < Ch ? static_cast<long long>(owner) * Ch + local
+                      : static_cast<long long>(2 * a.world - 1 - owner) * Ch + (local - Ch);
+  };
+  const long long q_hi = gpos(q0, a.rank, a.Sq) + 127;
+  const int tpb = a.Skv / kN;
+  const int chunks = a.zigzag ? 2 : 1;
+  const int tpc = tpb / chunks;
+  std::vector<std::pair<int, int>> r;
+  for (int s = 0; s < a.nblk; ++s) {
+    const int owner = ((a.rank - a.blk_offset - s) % a.world + a.world) % a.world;
+    for (int c = 0; c < chunks; ++c) {
+      const long long k0 = gpos(c * tpc * kN, owner, a.Skv);
+      if (k0 > q_hi) continue;
+      const long long n = std::min<long long>((q_hi - k0) / kN + 1, tpc);
+      const int beg = s * tpb + c * tpc;
+      r.emplace_back(beg, beg + static_cast<int>(n));
+    }
+  }
+  return r;
+}
+
+// nsplit for a causal launch with dynamic claiming: simulate the CTAs claiming
+// items in kernel order (chunk-major, then head-major units with the last
+// query tiles first) and keep the split with the shortest makespan.  An item
+// costs its visible tiles plus `overhead`; a split adds one merge pass.
+int causal_split(const FlashArgs& a, int kN, int units, int tiles, int sms, int overhead) {
+  static std::mutex mu;
+  static std::map<std::vector<long long>, int> cache;
+  const std::vector<long long> key{a.Sq, a.Skv,  a.nblk,       a.Hq,     a.world, a.rank,
+                                   a.blk_offset, a.zigzag, kN, sms,    overhead};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int per_head = a.Sq / 128;
+  std::vector<std::vector<std::pair<int, int>>> vis(per_head);
+  for (int qt = 0; qt < per_head; ++qt) vis[qt] = visible_ranges(a, kN, qt * 128);
+  int best = 1;
+  double best_span = 1e300;
+  for (int ns = 1; ns <= 16 && ns <= tiles; ++ns) {
+    const long long items = static_cast<long long>(units) * ns;
+    const int G = static_cast<int>(std::min<long long>(items, sms));
+    std::priority_queue<double, std::vector<double>, std::greater<double>> load;
+    for (int i = 0; i < G; ++i) load.push(0.0);
+    double span = 0.0;
+    for (int c = 0; c < ns; ++c) {
+      const int vb = static_cast<int>(static_cast<long long>(c) * tiles / ns);
+      const int ve = static_cast<int>(static_cast<long long>(c + 1) * tiles / ns);
+      for (int u = 0; u < units; ++u) {
+        const int qt = per_head - 1 - u % per_head;  // the kernel's unit order
+        int n = 0;
+        for (const auto& r : vis[qt]) n += std::max(0, std::min(r.second, ve) - std::max(r.first, vb));
+        const double t = load.top() + n + overhead;
+        load.pop();
+        load.push(t);
+        span = std::max(span, t);
+      }
+    }
+    if (ns > 1) span += 4;  // merge pass
+    if (span < best_span * 0.995) {
+      best_span = span;
+      best = ns;
+    }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 256) cache.clear();
+  cache[key] = best;
+  return best;
+}
+
 int tiles_of(const FlashArgs& a) { return a.nblk * (a.Skv / (a.prec == Prec::kF32x3 ? 64 : 128)); }
 
 }  // namespace
@@ -77,7 +160,13 @@ FlashPlan flash_plan(const FlashArgs& a) {
     pl.workspace_bytes = static_cast<size_t>(2 * pl.grid) * 128 * (a.D + 2) * sizeof(float);
     return pl;
   }
-  pl.nsplit = a.nsplit > 0 ? a.nsplit : flash_choose_split(pl.n_units, tiles, sms, overhead);
+  const bool dyn = a.causal && pl.rows_per_unit == 128 && dynamic_enabled();
+  if (a.nsplit > 0)
+    pl.nsplit = a.nsplit;
+  else if (dyn)
+    pl.nsplit = causal_split(a, a.prec == Prec::kF32x3 ? 64 : 128, pl.n_units, tiles, sms, overhead);
+  else
+    pl.nsplit = flash_choose_split(pl.n_units, tiles, sms, overhead);
   if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;
   pl.n_items = pl.n_units * pl.nsplit;
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
@@ -87,7 +176,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
                                      : 0;
   // causal items differ in cost: claim them dynamically (the two-tile kernel keeps its
   // static order)
-  pl.dynamic = (a.causal && pl.rows_per_unit == 128 && dynamic_enabled()) ? 1 : 0;
+  pl.dynamic = dyn ? 1 : 0;
   return pl;
 }
 
