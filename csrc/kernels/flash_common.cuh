@@ -131,22 +131,15 @@ __device__ __forceinline__ Item work_item(const FlashParams& p, int k, int tiles
   return it;
 }
 
-// Work item w of this CTA, false when the CTA has no more.  The static
-// schedules take the w-th entry of the CTA's precomputed list; the dynamic one
-// (p.dynamic) claims the next unclaimed item of the whole grid from a counter
-// in the status block (pad[0]), so a CTA that drew cheap items (short causal
-// query tiles) takes more of them.  Items are claimed in order, so the cheap
-// tail of the longest-first order balances the end of the schedule.
-__device__ __forceinline__ bool next_item(const FlashParams& p, int w, int tiles_total,
-                                          const int* sw, Item* it) {
-  if (p.dynamic) {
-    const uint32_t i = atomicAdd(&p.status->pad[0], 1u);
-    if (i >= static_cast<uint32_t>(p.n_items)) return false;
-    *it = make_item(p, static_cast<int>(i), tiles_total);
-    return true;
-  }
-  if (w >= sw[0]) return false;
-  *it = work_item(p, w, tiles_total, sw);
+// Dynamic schedule (p.dynamic): claim the next unclaimed equal-split item of
+// the whole grid from a counter in the status block (pad[0]); false once all
+// are taken.  A CTA that drew cheap items (short causal query tiles) takes
+// more of them, and since items are claimed in order, the cheap tail of the
+// longest-first unit order balances the end of the schedule.
+__device__ __forceinline__ bool claim_item(const FlashParams& p, int tiles_total, Item* it) {
+  const uint32_t i = atomicAdd(&p.status->pad[0], 1u);
+  if (i >= static_cast<uint32_t>(p.n_items)) return false;
+  *it = make_item(p, static_cast<int>(i), tiles_total);
   return true;
 }
 

@@ -92,7 +92,9 @@ struct Cfg {
                                                   kTF32 ? kMajorK : kMajorMN);
 };
 
-template <Prec P, int D>
+// kDyn: work items come from the dynamic claim counter through the in-CTA
+// queue (causal launches); otherwise every role walks the CTA's static list.
+template <Prec P, int D, bool kDyn>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ FlashParams p, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV) {
@@ -176,18 +178,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ready_blocks = 1;  // blocks [0, ready_blocks) known present locally
       bool ok = true;
       for (int w = 0; ok; ++w) {
-        // publish work item w (or the end marker) to the MMA and softmax roles
-        const int slot = w % kItemSlots;
-        if (w >= kItemSlots) {
-          ok = mbar_wait(&item_empty[slot], ((w / kItemSlots) - 1) & 1, st, kSiteItemQueue, tmo);
-          if (!ok) break;
-        }
         Item it;
-        const bool have = next_item(p, w, tiles_total, s_work, &it);
-        if (!have) it.unit = -1;
-        s_items[slot] = it;
-        mbar_arrive(&item_full[slot]);
-        if (!have) break;
+        if constexpr (kDyn) {
+          // claim item w and publish it (or the end marker) to the MMA and softmax roles
+          const int slot = w % kItemSlots;
+          if (w >= kItemSlots) {
+            ok = mbar_wait(&item_empty[slot], ((w / kItemSlots) - 1) & 1, st, kSiteItemQueue, tmo);
+            if (!ok) break;
+          }
+          const bool have = claim_item(p, tiles_total, &it);
+          if (!have) it.unit = -1;
+          s_items[slot] = it;
+          mbar_arrive(&item_full[slot]);
+          if (!have) break;
+        } else {
+          if (w >= s_work[0]) break;
+          it = work_item(p, w, tiles_total, s_work);
+        }
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
           int k_lo, q_lo;
           if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
@@ -253,12 +260,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       int final_count = 0;  // items that had at least one visible tile
       bool ok = true;
       for (int w = 0; ok; ++w, ++item_count) {
-        const int slot = w % kItemSlots;
-        ok = mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st, kSiteItemQueue, tmo);
-        if (!ok) break;
-        const Item it = s_items[slot];
-        mbar_arrive(&item_empty[slot]);  // the item now lives in registers
-        if (it.unit < 0) break;
+        Item it;
+        if constexpr (kDyn) {
+          const int slot = w % kItemSlots;
+          ok = mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st, kSiteItemQueue, tmo);
+          if (!ok) break;
+          it = s_items[slot];
+          mbar_arrive(&item_empty[slot]);  // the item now lives in registers
+          if (it.unit < 0) break;
+        } else {
+          if (w >= s_work[0]) break;
+          it = work_item(p, w, tiles_total, s_work);
+        }
         ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
         if (!ok) break;
         tc_fence_after();
@@ -375,11 +388,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int w = 0; ok; ++w, ++item_count) {
       const int slot = w % kItemSlots;
-      ok = __all_sync(0xffffffffu, mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st,
-                                             kSiteItemQueue, tmo));
-      if (!ok) break;
-      const Item it = s_items[slot];
-      if (it.unit < 0) break;
+      Item it;
+      if constexpr (kDyn) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st,
+                                               kSiteItemQueue, tmo));
+        if (!ok) break;
+        it = s_items[slot];
+        if (it.unit < 0) break;
+      } else {
+        if (w >= s_work[0]) break;
+        it = work_item(p, w, tiles_total, s_work);
+      }
       const int qrow = it.q0 + row;
       // ---- this warpgroup's half of the Q row -> TMEM ----
       {
@@ -539,8 +558,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t o_tm = tmem + lane_base + C::kColO + half * kHalfD;
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
-      // re-read here from the queue slot rather than kept live across the tile loop
-      const Item ie = s_items[slot];
+      // re-read here (queue slot or shared-memory work list) rather than kept live
+      // across the tile loop
+      const Item ie = kDyn ? s_items[slot] : work_item(p, w, tiles_total, s_work);
       const size_t r = static_cast<size_t>(ie.q0 + row) * p.Hq + ie.h;
       const bool split = ie.store >= 0;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
@@ -596,13 +616,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // all TMEM reads of this item are done before the next Q lands in TMEM
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&item_empty[slot]);  // queue slot free again
+      if constexpr (kDyn) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&item_empty[slot]);  // queue slot free again
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (p.dynamic && threadIdx.x == 0) {
+  if (kDyn && threadIdx.x == 0) {
     // Every CTA has stopped claiming items once it gets here; the last one
     // resets the claim counter for the next launch that uses this status block.
     __threadfence();
@@ -775,37 +797,41 @@ __global__ void split_vt_kernel(const float* __restrict__ v, float* __restrict__
   }
 }
 
-template <Prec P, int D>
-void set_smem_attr() {
-  using C = Cfg<P, D>;
-  cudaFuncSetAttribute(flash_fwd_kernel<P, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       C::kSmemBytes);
-}
-
-template <Prec P, int D>
-int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
-                cudaStream_t stream) {
+template <Prec P, int D, bool kDyn>
+int launch_one(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
+               cudaStream_t stream) {
   using C = Cfg<P, D>;
   // the shared-memory opt-in is a per-device function attribute
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    set_smem_attr<P, D>();
+    cudaFuncSetAttribute(flash_fwd_kernel<P, D, kDyn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         C::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  if (p.Skv % C::kN != 0)
-    throw std::runtime_error("flash: keys per block must be a multiple of " +
-                             std::to_string(C::kN));
   if (cooperative) {
     void* args[] = {const_cast<FlashParams*>(&p), const_cast<CUtensorMap*>(&maps.k),
                     const_cast<CUtensorMap*>(&maps.v)};
     return static_cast<int>(cudaLaunchCooperativeKernel(
-        reinterpret_cast<void*>(flash_fwd_kernel<P, D>), dim3(grid), dim3(kThreads), args,
+        reinterpret_cast<void*>(flash_fwd_kernel<P, D, kDyn>), dim3(grid), dim3(kThreads), args,
         C::kSmemBytes, stream));
   }
-  flash_fwd_kernel<P, D><<<grid, kThreads, C::kSmemBytes, stream>>>(p, maps.k, maps.v);
+  flash_fwd_kernel<P, D, kDyn><<<grid, kThreads, C::kSmemBytes, stream>>>(p, maps.k, maps.v);
   return static_cast<int>(cudaGetLastError());
+}
+
+template <Prec P, int D>
+int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
+                cudaStream_t stream) {
+  using C = Cfg<P, D>;
+  if (p.Skv % C::kN != 0)
+    throw std::runtime_error("flash: keys per block must be a multiple of " +
+                             std::to_string(C::kN));
+  if (p.dynamic && p.balanced)
+    throw std::runtime_error("flash: the dynamic and balanced schedules exclude each other");
+  return p.dynamic ? launch_one<P, D, true>(p, maps, grid, cooperative, stream)
+                   : launch_one<P, D, false>(p, maps, grid, cooperative, stream);
 }
 
 }  // namespace
