@@ -92,9 +92,12 @@ struct Cfg {
                                                   kTF32 ? kMajorK : kMajorMN);
 };
 
-// kDyn: work items come from the dynamic claim counter through the in-CTA
-// queue (causal launches); otherwise every role walks the CTA's static list.
-template <Prec P, int D, bool kDyn>
+// kCausal: causal launch.  Its work items reach the MMA and softmax roles
+// through the in-CTA queue (claimed from the dynamic counter when p.dynamic,
+// else from the static list), and tiles are classified against the mask.  A
+// non-causal instantiation has no classification at all and every role walks
+// the CTA's static (or balanced) list itself.
+template <Prec P, int D, bool kCausal>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ FlashParams p, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV) {
@@ -179,14 +182,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int w = 0; ok; ++w) {
         Item it;
-        if constexpr (kDyn) {
-          // claim item w and publish it (or the end marker) to the MMA and softmax roles
+        if constexpr (kCausal) {
+          // take item w and publish it (or the end marker) to the MMA and softmax roles
           const int slot = w % kItemSlots;
           if (w >= kItemSlots) {
             ok = mbar_wait(&item_empty[slot], ((w / kItemSlots) - 1) & 1, st, kSiteItemQueue, tmo);
             if (!ok) break;
           }
-          const bool have = claim_item(p, tiles_total, &it);
+          bool have;
+          if (p.dynamic) {
+            have = claim_item(p, tiles_total, &it);
+          } else {
+            have = w < s_work[0];
+            if (have) it = work_item(p, w, tiles_total, s_work);
+          }
           if (!have) it.unit = -1;
           s_items[slot] = it;
           mbar_arrive(&item_full[slot]);
@@ -196,8 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           it = work_item(p, w, tiles_total, s_work);
         }
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          int k_lo, q_lo;
-          if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if constexpr (kCausal) {
+            int k_lo, q_lo;
+            if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          }
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int w = 0; ok; ++w, ++item_count) {
         Item it;
-        if constexpr (kDyn) {
+        if constexpr (kCausal) {
           const int slot = w % kItemSlots;
           ok = mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st, kSiteItemQueue, tmo);
           if (!ok) break;
@@ -316,8 +327,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           return true;
         };
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          int k_lo, q_lo;
-          if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          if constexpr (kCausal) {
+            int k_lo, q_lo;
+            if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
+          }
           const int stage = g % NS;
           const int b = g & 1;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
@@ -389,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; ok; ++w, ++item_count) {
       const int slot = w % kItemSlots;
       Item it;
-      if constexpr (kDyn) {
+      if constexpr (kCausal) {
         ok = __all_sync(0xffffffffu, mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st,
                                                kSiteItemQueue, tmo));
         if (!ok) break;
@@ -445,8 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
         int k_lo = 0, q_lo = 0;
-        const int cls = classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo);
-        if (cls == 0) continue;  // v moved to the end of the masked run
+        int cls = 1;
+        if constexpr (kCausal) {
+          cls = classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo);
+          if (cls == 0) continue;  // v moved to the end of the masked run
+        }
         const int b = g & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo));
         if (!ok) break;
@@ -560,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
       // re-read here (queue slot or shared-memory work list) rather than kept live
       // across the tile loop
-      const Item ie = kDyn ? s_items[slot] : work_item(p, w, tiles_total, s_work);
+      const Item ie = kCausal ? s_items[slot] : work_item(p, w, tiles_total, s_work);
       const size_t r = static_cast<size_t>(ie.q0 + row) * p.Hq + ie.h;
       const bool split = ie.store >= 0;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
@@ -616,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // all TMEM reads of this item are done before the next Q lands in TMEM
       tc_fence_before();
-      if constexpr (kDyn) {
+      if constexpr (kCausal) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&item_empty[slot]);  // queue slot free again
       }
@@ -624,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (kDyn && threadIdx.x == 0) {
+  if (kCausal && p.dynamic && threadIdx.x == 0) {
     // Every CTA has stopped claiming items once it gets here; the last one
     // resets the claim counter for the next launch that uses this status block.
     __threadfence();
@@ -797,7 +813,7 @@ __global__ void split_vt_kernel(const float* __restrict__ v, float* __restrict__
   }
 }
 
-template <Prec P, int D, bool kDyn>
+template <Prec P, int D, bool kCausal>
 int launch_one(const FlashParams& p, const FlashMaps& maps, int grid, bool cooperative,
                cudaStream_t stream) {
   using C = Cfg<P, D>;
@@ -806,7 +822,7 @@ int launch_one(const FlashParams& p, const FlashMaps& maps, int grid, bool coope
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    cudaFuncSetAttribute(flash_fwd_kernel<P, D, kDyn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(flash_fwd_kernel<P, D, kCausal>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          C::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
@@ -814,10 +830,10 @@ int launch_one(const FlashParams& p, const FlashMaps& maps, int grid, bool coope
     void* args[] = {const_cast<FlashParams*>(&p), const_cast<CUtensorMap*>(&maps.k),
                     const_cast<CUtensorMap*>(&maps.v)};
     return static_cast<int>(cudaLaunchCooperativeKernel(
-        reinterpret_cast<void*>(flash_fwd_kernel<P, D, kDyn>), dim3(grid), dim3(kThreads), args,
+        reinterpret_cast<void*>(flash_fwd_kernel<P, D, kCausal>), dim3(grid), dim3(kThreads), args,
         C::kSmemBytes, stream));
   }
-  flash_fwd_kernel<P, D, kDyn><<<grid, kThreads, C::kSmemBytes, stream>>>(p, maps.k, maps.v);
+  flash_fwd_kernel<P, D, kCausal><<<grid, kThreads, C::kSmemBytes, stream>>>(p, maps.k, maps.v);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -828,10 +844,10 @@ int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool coop
   if (p.Skv % C::kN != 0)
     throw std::runtime_error("flash: keys per block must be a multiple of " +
                              std::to_string(C::kN));
-  if (p.dynamic && p.balanced)
-    throw std::runtime_error("flash: the dynamic and balanced schedules exclude each other");
-  return p.dynamic ? launch_one<P, D, true>(p, maps, grid, cooperative, stream)
-                   : launch_one<P, D, false>(p, maps, grid, cooperative, stream);
+  if (p.dynamic && (p.balanced || !p.causal))
+    throw std::runtime_error("flash: the dynamic schedule is for causal equal-split launches");
+  return p.causal ? launch_one<P, D, true>(p, maps, grid, cooperative, stream)
+                  : launch_one<P, D, false>(p, maps, grid, cooperative, stream);
 }
 
 }  // namespace
