@@ -234,8 +234,8 @@ def main() -> int:
                            "streams; K-step loop timed as a whole"}
 
     nsplit = attn.engine.nsplit
-    # ring-format prep (fp32), the fused kernel, the merge pass (split or balanced)
-    per_step = (2 if dt == "fp32" else 0) + 1 + (1 if nsplit != 1 else 0)
+    # ring-format prep (fp32, one launch), the fused kernel, the merge pass (split or balanced)
+    per_step = (1 if dt == "fp32" else 0) + 1 + (1 if nsplit != 1 else 0)
     if rank == 0:
         line = {
             "metric": METRIC,

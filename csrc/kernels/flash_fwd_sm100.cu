@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 #include <cstring>
@@ -779,37 +780,45 @@ __device__ __forceinline__ void tf32_pair(float x, float& b, float& s) {
   s = __uint_as_float(ss);
 }
 
-__global__ void split_k_kernel(const float4* __restrict__ k, float4* __restrict__ kb,
-                               float4* __restrict__ ks, size_t n4) {
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const float4 x = k[i];
-    float4 b, s;
-    tf32_pair(x.x, b.x, s.x);
-    tf32_pair(x.y, b.y, s.y);
-    tf32_pair(x.z, b.z, s.z);
-    tf32_pair(x.w, b.w, s.w);
-    kb[i] = b;
-    ks[i] = s;
+// One launch formats a whole fp32 ring block (the split was two launches; the
+// per-step launch gap showed in the step time):
+//   blocks [0, n_vt):  V [Skv][Hkv][D] -> V^T planes [2][Hkv][D][Skv], one 32x32
+//                      tile each, transposed through shared memory;
+//   blocks [n_vt, ..): K [Skv][Hkv][D] -> planes [2][Skv][Hkv][D], float4 grid-stride.
+// Block shape (32, 8).
+__global__ void __launch_bounds__(256) ring_format_f32_kernel(
+    const float4* __restrict__ k, float4* __restrict__ kb, float4* __restrict__ ks, size_t n4,
+    const float* __restrict__ v, float* __restrict__ vt, int Skv, int Hkv, int D, int n_vt) {
+  if (static_cast<int>(blockIdx.x) < n_vt) {
+    __shared__ float tile[32][33];
+    const int sx = Skv / 32, dy = D / 32;
+    const int hk = blockIdx.x / (sx * dy);
+    const int rem = blockIdx.x - hk * (sx * dy);
+    const int s0 = (rem % sx) * 32, d0 = (rem / sx) * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y)
+      tile[i][threadIdx.x] = v[(static_cast<size_t>(s0 + i) * Hkv + hk) * D + d0 + threadIdx.x];
+    __syncthreads();
+    const size_t plane = static_cast<size_t>(Hkv) * D * Skv;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      float b, sm;
+      tf32_pair(tile[threadIdx.x][i], b, sm);
+      const size_t o = (static_cast<size_t>(hk) * D + d0 + i) * Skv + s0 + threadIdx.x;
+      vt[o] = b;
+      vt[plane + o] = sm;
+    }
+    return;
   }
-}
-
-// V [Skv][Hkv][D] -> VT planes [2][Hkv][D][Skv]; 32x32 tiles through shared memory.
-__global__ void split_vt_kernel(const float* __restrict__ v, float* __restrict__ vt, int Skv,
-                                int Hkv, int D) {
-  __shared__ float tile[32][33];
-  const int hk = blockIdx.z;
-  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y)
-    tile[i][threadIdx.x] = v[(static_cast<size_t>(s0 + i) * Hkv + hk) * D + d0 + threadIdx.x];
-  __syncthreads();
-  const size_t plane = static_cast<size_t>(Hkv) * D * Skv;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    float b, s;
-    tf32_pair(tile[threadIdx.x][i], b, s);
-    const size_t o = (static_cast<size_t>(hk) * D + d0 + i) * Skv + s0 + threadIdx.x;
-    vt[o] = b;
-    vt[plane + o] = s;
+  const size_t nb = gridDim.x - n_vt;
+  const size_t t = threadIdx.y * 32 + threadIdx.x;
+  for (size_t i = (blockIdx.x - n_vt) * static_cast<size_t>(256) + t; i < n4; i += nb * 256) {
+    const float4 x = k[i];
+    float4 b, sm;
+    tf32_pair(x.x, b.x, sm.x);
+    tf32_pair(x.y, b.y, sm.y);
+    tf32_pair(x.z, b.z, sm.z);
+    tf32_pair(x.w, b.w, sm.w);
+    kb[i] = b;
+    ks[i] = sm;
   }
 }
 
@@ -997,15 +1006,14 @@ int ring_format_launch(Prec prec, const void* k, const void* v, void* k_dst, voi
   }
   if (Skv % 32 != 0 || D % 32 != 0) throw std::runtime_error("ring_format: Skv, D % 32");
   const size_t n4 = e / 4;
-  int blocks = static_cast<int>((n4 + 255) / 256);
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  const long long n_vt = static_cast<long long>(Skv / 32) * (D / 32) * Hkv;
+  const long long n_k = std::min<long long>((n4 + 255) / 256, 148 * 8);
+  if (n_vt + n_k > 0x7fffffffLL) throw std::runtime_error("ring_format: block too large");
   float* kb = static_cast<float*>(k_dst);
-  split_k_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float4*>(k),
-                                             reinterpret_cast<float4*>(kb),
-                                             reinterpret_cast<float4*>(kb + e), n4);
-  dim3 g2(Skv / 32, D / 32, Hkv), b2(32, 8);
-  split_vt_kernel<<<g2, b2, 0, stream>>>(static_cast<const float*>(v), static_cast<float*>(v_dst),
-                                         Skv, Hkv, D);
+  ring_format_f32_kernel<<<static_cast<unsigned>(n_vt + n_k), dim3(32, 8), 0, stream>>>(
+      static_cast<const float4*>(k), reinterpret_cast<float4*>(kb),
+      reinterpret_cast<float4*>(kb + e), n4, static_cast<const float*>(v),
+      static_cast<float*>(v_dst), Skv, Hkv, D, static_cast<int>(n_vt));
   return static_cast<int>(cudaGetLastError());
 }
 
