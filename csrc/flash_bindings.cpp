@@ -3,6 +3,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+#include <pybind11/stl.h>
 
 #include "flash.h"
 
@@ -102,7 +103,73 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
 }  // namespace
 }  // namespace rab
 
+namespace rab {
+namespace {
+
+// Host-only view of the planner (no GPU needed when sms > 0).
+FlashArgs plan_args(int64_t prec, int64_t Sq, int64_t Skv, int64_t nblk, int64_t Hq, int64_t Hkv,
+                    int64_t D, bool causal, bool zigzag, int64_t world, int64_t rank,
+                    int64_t blk_offset, int64_t nsplit, int64_t sms, bool fused) {
+  FlashArgs a;
+  a.prec = to_prec(prec);
+  a.Sq = static_cast<int>(Sq);
+  a.Skv = static_cast<int>(Skv);
+  a.nblk = static_cast<int>(nblk);
+  a.Hq = static_cast<int>(Hq);
+  a.Hkv = static_cast<int>(Hkv);
+  a.D = static_cast<int>(D);
+  a.causal = causal;
+  a.zigzag = zigzag;
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.blk_offset = static_cast<int>(blk_offset);
+  a.nsplit = static_cast<int>(nsplit);
+  a.sms = static_cast<int>(sms);
+  a.fused = fused;
+  return a;
+}
+
+}  // namespace
+}  // namespace rab
+
 void register_flash(pybind11::module_& m) {
+  m.def(
+      "flash_plan_info",
+      [](int64_t prec, int64_t Sq, int64_t Skv, int64_t nblk, int64_t Hq, int64_t Hkv, int64_t D,
+         bool causal, bool zigzag, int64_t world, int64_t rank, int64_t blk_offset, int64_t nsplit,
+         int64_t sms, bool fused) {
+        const rab::FlashPlan pl = rab::flash_plan(rab::plan_args(
+            prec, Sq, Skv, nblk, Hq, Hkv, D, causal, zigzag, world, rank, blk_offset, nsplit, sms,
+            fused));
+        pybind11::dict d;
+        d["rows_per_unit"] = pl.rows_per_unit;
+        d["nsplit"] = pl.nsplit;
+        d["balanced"] = pl.balanced;
+        d["full_waves"] = pl.full_waves;
+        d["dynamic"] = pl.dynamic;
+        d["n_units"] = pl.n_units;
+        d["n_items"] = pl.n_items;
+        d["grid"] = pl.grid;
+        d["workspace_bytes"] = pl.workspace_bytes;
+        return d;
+      },
+      pybind11::arg("prec"), pybind11::arg("Sq"), pybind11::arg("Skv"), pybind11::arg("nblk"),
+      pybind11::arg("Hq"), pybind11::arg("Hkv"), pybind11::arg("D"), pybind11::arg("causal") = false,
+      pybind11::arg("zigzag") = false, pybind11::arg("world") = 1, pybind11::arg("rank") = 0,
+      pybind11::arg("blk_offset") = 0, pybind11::arg("nsplit") = 0, pybind11::arg("sms") = 0,
+      pybind11::arg("fused") = false);
+  m.def(
+      "flash_visible_ranges",
+      [](int64_t prec, int64_t Sq, int64_t Skv, int64_t nblk, bool zigzag, int64_t world,
+         int64_t rank, int64_t blk_offset, int64_t q0) {
+        return rab::flash_visible_ranges(
+            rab::plan_args(prec, Sq, Skv, nblk, 1, 1, 64, true, zigzag, world, rank, blk_offset, 0,
+                           1, false),
+            static_cast<int>(q0));
+      },
+      pybind11::arg("prec"), pybind11::arg("Sq"), pybind11::arg("Skv"), pybind11::arg("nblk"),
+      pybind11::arg("zigzag"), pybind11::arg("world"), pybind11::arg("rank"),
+      pybind11::arg("blk_offset") = 0, pybind11::arg("q0") = 0);
   m.def("ring_block_bytes", [](int64_t prec, int64_t Skv, int64_t Hkv, int64_t D) {
     return static_cast<int64_t>(rab::ring_block_bytes(static_cast<rab::Prec>(prec), Skv, Hkv, D));
   });

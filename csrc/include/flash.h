@@ -10,6 +10,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
+#include <vector>
 
 #include "host_comm.h"
 #include "status.h"
@@ -152,6 +154,7 @@ struct FlashArgs {
   void* workspace = nullptr;         // split partials (see flash_workspace_bytes)
   size_t workspace_bytes = 0;
   int grid = 0;                      // <= 0: min(items, SMs)
+  int sms = 0;                       // > 0: plan for this many SMs (default: the current device's)
   DeviceStatus* status = nullptr;
   double timeout_s = 10.0;
   // fused ring transfer
@@ -180,6 +183,10 @@ struct FlashPlan {
 };
 
 FlashPlan flash_plan(const FlashArgs& a);
+
+// Visible KV tiles of the 128-row query tile at local row q0 under the causal
+// mask, as [begin, end) ranges of ring tile indices (the planner's closed form).
+std::vector<std::pair<int, int>> flash_visible_ranges(const FlashArgs& a, int q0);
 int flash_run(const FlashArgs& a, const FlashPlan& plan, cudaStream_t stream);
 
 }  // namespace rab

@@ -133,6 +133,10 @@ int tiles_of(const FlashArgs& a) { return a.nblk * (a.Skv / (a.prec == Prec::kF3
 
 }  // namespace
 
+std::vector<std::pair<int, int>> flash_visible_ranges(const FlashArgs& a, int q0) {
+  return visible_ranges(a, a.prec == Prec::kF32x3 ? 64 : 128, q0);
+}
+
 FlashPlan flash_plan(const FlashArgs& a) {
   if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
   FlashPlan pl{};
@@ -140,7 +144,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.rows_per_unit = (a.prec == Prec::kBF16 && a.Sq % 256 == 0 && two_tile_enabled()) ? 256 : 128;
   pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
   const int tiles = tiles_of(a);
-  const int sms = flash_sm_count();
+  const int sms = a.sms > 0 ? a.sms : flash_sm_count();
   // per-item overhead in tiles: ~6 of the fp32 kernel's 64-key tiles, ~3 of 128-key bf16 tiles
   const int overhead = a.prec == Prec::kF32x3 ? 6 : 3;
   // the balanced schedule needs equal-cost tiles (no causal mask) and 128-row units

@@ -1,0 +1,94 @@
+"""Host planner of the flash kernel, on the CPU (no GPU: the SM count is given).
+
+* The causal planner's closed-form visible tile ranges against a brute-force
+  classification of every (query tile, KV tile) pair by global position, with
+  contiguous and zigzag sharding, several ranks and ring block offsets.
+* The schedule choices the kernel relies on: the balanced schedule for the
+  headline 16384 x 1 head fp32 workload, equal split for many heads, dynamic
+  claiming with a split for long causal rows, and the forced modes.
+"""
+import pytest
+
+from ring_attention_benchmark_b200._ext import load
+from ring_attention_benchmark_b200.models import oracle
+
+F32, BF16 = 1, 0
+
+
+@pytest.fixture(scope="module")
+def C():
+    try:
+        return load()
+    except Exception as e:  # pragma: no cover - extension not built
+        pytest.skip(f"extension not built: {e}")
+
+
+def _brute_visible(prec, sq, skv, nblk, zigzag, world, rank, blk_offset, q0):
+    kN = 64 if prec == F32 else 128
+    tpb = skv // kN
+
+    def pos(owner, n, i):
+        if zigzag:
+            return int(oracle.zigzag_positions(owner, world, n)[i])
+        return owner * n + i
+
+    q_hi = pos(rank, sq, q0 + 127)
+    vis = set()
+    for s in range(nblk):
+        owner = (rank - blk_offset - s) % world
+        for t in range(tpb):
+            if pos(owner, skv, t * kN) <= q_hi:
+                vis.add(s * tpb + t)
+    return vis
+
+
+@pytest.mark.parametrize("prec", [F32, BF16])
+@pytest.mark.parametrize("zigzag", [False, True])
+@pytest.mark.parametrize("world,rank,blk_offset", [(1, 0, 0), (2, 1, 0), (4, 2, 0), (4, 3, 1)])
+def test_visible_ranges_match_bruteforce(C, prec, zigzag, world, rank, blk_offset):
+    sq = skv = 1024
+    nblk = world - blk_offset
+    for q0 in range(0, sq, 128):
+        ranges = C.flash_visible_ranges(prec, sq, skv, nblk, zigzag, world, rank, blk_offset, q0)
+        got = set()
+        for a, b in ranges:
+            assert a < b
+            got.update(range(a, b))
+        assert got == _brute_visible(prec, sq, skv, nblk, zigzag, world, rank, blk_offset, q0), \
+            (q0, ranges)
+
+
+def test_plan_headline_is_balanced(C):
+    # 16384 tokens x 1 head: 128 query tiles would leave 20 of 148 SMs idle
+    pl = C.flash_plan_info(F32, 16384, 16384, 1, 1, 1, 64, sms=148)
+    assert pl["balanced"] == 1 and pl["grid"] == 148 and pl["n_items"] == 148
+    assert pl["full_waves"] == 0 and pl["dynamic"] == 0
+    # two partial records (acc [128][64] + m + l) per CTA
+    assert pl["workspace_bytes"] == 2 * 148 * 128 * (64 + 2) * 4
+    # eight ring blocks: still balanced, every CTA also copies its slice
+    pl8 = C.flash_plan_info(F32, 16384, 16384, 8, 1, 1, 64, sms=148, fused=True)
+    assert pl8["balanced"] == 1 and pl8["grid"] == 148
+
+
+def test_plan_many_heads_equal_split(C):
+    pl = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, sms=148)
+    assert pl["balanced"] == 0 and pl["nsplit"] == 1 and pl["n_items"] == 4096
+    assert pl["grid"] == 148 and pl["workspace_bytes"] == 0
+
+
+def test_plan_causal_is_dynamic(C):
+    # long causal rows on one head: a split shortens the longest query tile
+    pl = C.flash_plan_info(F32, 16384, 16384, 1, 1, 1, 64, causal=True, sms=148)
+    assert pl["dynamic"] == 1 and pl["balanced"] == 0 and pl["nsplit"] == 2
+    # many heads: enough items without a split
+    pl = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True, sms=148)
+    assert pl["dynamic"] == 1 and pl["nsplit"] == 1
+
+
+def test_plan_forced_modes(C):
+    pl = C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=-1, sms=148)
+    assert pl["balanced"] == 1 and pl["full_waves"] == 1  # 256 units: one whole wave first
+    pl = C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=3, sms=148)
+    assert pl["balanced"] == 0 and pl["nsplit"] == 3 and pl["n_items"] == 768
+    with pytest.raises(RuntimeError, match="balanced"):
+        C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, causal=True, nsplit=-1, sms=148)
