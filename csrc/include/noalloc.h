@@ -17,8 +17,10 @@
 //    out [Sq, Hq, D], all bf16, contiguous, on the current device; lse
 //    [Sq, Hq] fp32 or NULL.  D is 64 or 128, Sq a multiple of 128, Skv a
 //    multiple of 128, Hq a multiple of Hkv.
-//  * nsplit = 0 picks the KV split the regular entry point would pick.  A
-//    problem whose split workspace exceeds the scratch array is rejected with
+//  * nsplit = 0 picks an equal KV split from the wave cost model (the
+//    regular entry point may pick its balanced or causal-aware schedule
+//    instead; the results agree within bf16 rounding).  A problem whose split
+//    workspace exceeds the scratch array is rejected with
 //    RAB_NOALLOC_ERR_TOO_LARGE and a message in `err` - it is not shrunk.
 //  * no cudaMalloc, cudaFree or allocating library call is made.  The first
 //    call on a device resolves the scratch array's device address once
