@@ -222,6 +222,21 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // tcgen05.ld / st, shape 32x32b: each thread of the warp owns one TMEM lane
 // (lane = 32*(warp%4) + laneid) and moves N consecutive 32-bit columns.
 // ---------------------------------------------------------------------------
+// Warpgroup register reallocation (every thread of the warpgroup executes it).
+// `inc` waits until the block's pool has the registers, so the warpgroups'
+// shares must add up to at most the registers the block was launched with and
+// every `dec` must run unconditionally.
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_dec() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_inc() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

@@ -13,7 +13,11 @@
 //   warp 1      MMA issuer (one thread) and TMEM owner
 //   warps 2-3   ring copy warps (fused mode), shared with the one-tile kernel
 //   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: one thread per
-//               query row, full rows, in two passes over the S row in TMEM
+//               query row, the full 128-column S row in registers (one pass)
+// Registers: warpgroup 0 (warps 0-3) gives up registers after start-up
+// (setmaxnreg.dec to kRegsLow) and the two softmax warpgroups take them
+// (setmaxnreg.inc to kRegsHigh); 128 * kRegsLow + 256 * kRegsHigh stays within
+// the 168 * 384 registers the block is launched with.
 // TMEM: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [384,384+D); P is
 // written back over S as packed bf16 (A operand of the PV MMA).
 // Every wait is bounded; no TMA load uses cluster broadcast.
@@ -43,6 +47,11 @@ constexpr int kWMma = 1;
 constexpr int kWComm = 2;
 constexpr int kWSoft = 4;  // warps 4..7 tile A, 8..11 tile B
 constexpr uint32_t kCols = 512;
+constexpr uint32_t kRegsLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
+constexpr uint32_t kRegsLow = 72;      // warpgroup 0: TMA, MMA, ring copy
+constexpr uint32_t kRegsHigh = 216;    // softmax warpgroups
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kRegsLaunch * 384,
+              "register split exceeds the launch allocation");
 
 template <int D>
 struct Cfg2 {
@@ -74,7 +83,9 @@ __device__ __forceinline__ bool visible2(const FlashParams& p, int q0, int* v_io
   return classify(p, q0 + kM, v_io, 128, tpb, &a, &b) != 0;
 }
 
-template <int D>
+// kCausal: tiles are classified against the causal mask; a non-causal
+// instantiation treats every tile as full.
+template <int D, bool kCausal>
 __global__ void __launch_bounds__(kThreads2, 1)
     flash_fwd_2q_kernel(const __grid_constant__ FlashParams p,
                         const __grid_constant__ CUtensorMap tmQ,
@@ -135,7 +146,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const uint32_t tmem = tmem_slot;
   const int tpb = p.Skv / kN;
   const int tiles_total = p.nblk * tpb;
-
+  if (warp < 4) {
+  // warpgroup 0 gives up registers first thing, unconditionally: the softmax
+  // warpgroups' increase below is served by this decrease
+  warpgroup_reg_dec<kRegsLow>();
   if (warp == kWTma) {
     // ------------------------------------------------------------------ TMA
     if (elect_one()) {
@@ -156,7 +170,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
             tma_load_3d(sQ + x * C::kQTile + ds * (kM * 128), &tmQ, q_full, ds * 64, it.h,
                         it.q0 + x * kM);
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if (!visible2(p, it.q0, &v, tpb)) continue;
+          if constexpr (kCausal) {
+            if (!visible2(p, it.q0, &v, tpb)) continue;
+          }
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
@@ -234,7 +250,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tc_fence_after();
         int j = 0;
         for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if (!visible2(p, it.q0, &v, tpb)) continue;
+          if constexpr (kCausal) {
+            if (!visible2(p, it.q0, &v, tpb)) continue;
+          }
           const int stage = g % NS;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
           if (!ok) break;
@@ -260,9 +278,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mma_commit(drain);
       mbar_wait(drain, 0, nullptr, kSiteOReady, 1000000000ull);
     }
-  } else if (warp == kWComm || warp == kWComm + 1) {
-    if (p.fused && p.world > 1) ring_copy_role(p, threadIdx.x - kWComm * 32, &s_copy_ok);
   } else {
+    if (p.fused && p.world > 1) ring_copy_role(p, threadIdx.x - kWComm * 32, &s_copy_ok);
+  }
+  } else {
+    warpgroup_reg_inc<kRegsHigh>();
     // -------------------------------------------------------------- softmax
     const int x = (warp - kWSoft) >> 2;             // query tile of this warpgroup
     const int row = (threadIdx.x - kWSoft * 32) & 127;
@@ -279,27 +299,32 @@ __global__ void __launch_bounds__(kThreads2, 1)
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-        if (!visible2(p, it.q0, &v, tpb)) continue;
-        int k_lo = 0, q_lo = 0;
-        int vq = v;  // this query tile's own classification; v itself is visible to the unit
-        const int cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
-        const int lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);  // visible cols <= lim
+        int lim = kN;  // visible columns: c <= lim
+        if constexpr (kCausal) {
+          if (!visible2(p, it.q0, &v, tpb)) continue;
+          int k_lo = 0, q_lo = 0;
+          int vq = v;  // this query tile's own classification; v itself is visible to the unit
+          const int cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
+          lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);
+        }
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], g & 1, st, kSiteSFull, tmo));
         if (!ok) break;
         tc_fence_after();
-        // pass 1: row max
+        // the whole S row of this thread in registers
+        uint32_t sr[kN];
+#pragma unroll
+        for (int c = 0; c < kN; c += 32) tmem_ld32(s_col + c, sr + c);
+        tmem_ld_wait();
+        if constexpr (kCausal) {
+#pragma unroll
+          for (int c = 0; c < kN; ++c)
+            if (c > lim) sr[c] = 0xff800000u;  // -inf
+        }
         float pm[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
+        for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sr[i]);
 #pragma unroll
-        for (int c = 0; c < kN; c += 32) {
-          uint32_t sr[32];
-          tmem_ld32(s_col + c, sr);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c + i <= lim) pm[i & 7] = fmaxf(pm[i & 7], __uint_as_float(sr[i]));
-        }
+        for (int c = 8; c < kN; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
         const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
         const bool need = mx > m_run + kRescaleThreshold;
@@ -326,24 +351,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        // pass 2: exponentials, row sum, packed bf16 P over S
+        // exponentials, row sum, packed bf16 P over the first 64 S columns
         float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[kN / 2];
 #pragma unroll
-        for (int c = 0; c < kN; c += 32) {
-          // packed columns c/2 .. c/2+15 hold S columns already read
-          uint32_t sa[32], pk[16];
-          tmem_ld32(s_col + c, sa);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int c0 = c + 2 * i, c1 = c0 + 1;
-            const float e0 = c0 <= lim ? ex2_approx(fmaf(__uint_as_float(sa[2 * i]), sl2, -m_use)) : 0.f;
-            const float e1 = c1 <= lim ? ex2_approx(fmaf(__uint_as_float(sa[2 * i + 1]), sl2, -m_use)) : 0.f;
-            ps8[i & 7] += e0 + e1;
-            pk[i] = pack_bf16x2(e0, e1);
-          }
-          tmem_st16(s_col + c / 2, pk);
+        for (int i = 0; i < kN / 2; ++i) {
+          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -m_use));
+          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -m_use));
+          ps8[i & 7] += e0 + e1;
+          pk[i] = pack_bf16x2(e0, e1);
         }
+#pragma unroll
+        for (int c = 0; c < kN / 2; c += 32) tmem_st32(s_col + c, pk + c);
         l_run += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
         tmem_st_wait();
         tc_fence_before();
@@ -424,7 +443,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   }
 }
 
-template <int D>
+template <int D, bool kCausal>
 int launch2(const FlashParams& p, const CUtensorMap& tq, const FlashMaps& maps, int grid,
             bool cooperative, cudaStream_t stream) {
   using C = Cfg2<D>;
@@ -432,18 +451,18 @@ int launch2(const FlashParams& p, const CUtensorMap& tq, const FlashMaps& maps, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    cudaFuncSetAttribute(flash_fwd_2q_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         C::kSmemBytes);
+    cudaFuncSetAttribute(flash_fwd_2q_kernel<D, kCausal>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
   if (cooperative) {
     void* args[] = {const_cast<FlashParams*>(&p), const_cast<CUtensorMap*>(&tq),
                     const_cast<CUtensorMap*>(&maps.k), const_cast<CUtensorMap*>(&maps.v)};
     return static_cast<int>(cudaLaunchCooperativeKernel(
-        reinterpret_cast<void*>(flash_fwd_2q_kernel<D>), dim3(grid), dim3(kThreads2), args,
+        reinterpret_cast<void*>(flash_fwd_2q_kernel<D, kCausal>), dim3(grid), dim3(kThreads2), args,
         C::kSmemBytes, stream));
   }
-  flash_fwd_2q_kernel<D><<<grid, kThreads2, C::kSmemBytes, stream>>>(p, tq, maps.k, maps.v);
+  flash_fwd_2q_kernel<D, kCausal><<<grid, kThreads2, C::kSmemBytes, stream>>>(p, tq, maps.k, maps.v);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -461,8 +480,12 @@ int flash_forward_2q_launch(const FlashParams& p, const CUtensorMap& tq, const F
   if (p.rows_per_unit != 256 || p.Sq % 256 != 0)
     throw std::runtime_error("flash 2q: needs 256-row units");
   if (p.Skv % 128 != 0) throw std::runtime_error("flash 2q: keys per block must be a multiple of 128");
-  if (p.D == 64) return launch2<64>(p, tq, maps, grid, cooperative, stream);
-  if (p.D == 128) return launch2<128>(p, tq, maps, grid, cooperative, stream);
+  if (p.D == 64)
+    return p.causal ? launch2<64, true>(p, tq, maps, grid, cooperative, stream)
+                    : launch2<64, false>(p, tq, maps, grid, cooperative, stream);
+  if (p.D == 128)
+    return p.causal ? launch2<128, true>(p, tq, maps, grid, cooperative, stream)
+                    : launch2<128, false>(p, tq, maps, grid, cooperative, stream);
   throw std::runtime_error("flash 2q: head_dim must be 64 or 128");
 }
 

@@ -44,9 +44,19 @@ bool dynamic_enabled() {
   return e == nullptr || std::strcmp(e, "0") != 0;
 }
 
-bool two_tile_enabled() {
+// Two-query-tile bf16 kernel: RAB_FLASH_2Q=1 forces it (where the query rows
+// split into 256-row units), RAB_FLASH_2Q=0 disables it.  By default a
+// non-causal bf16 launch uses it when its 256-row units fill at least two
+// waves of the GPU (measured on B200: 4-10 % above the one-tile kernel there);
+// causal launches keep the one-tile kernel's dynamic claiming, small problems
+// its balanced schedule.
+bool use_two_tile(const FlashArgs& a, int sms) {
+  if (a.prec != Prec::kBF16 || a.Sq % 256 != 0) return false;
   const char* e = std::getenv("RAB_FLASH_2Q");
-  return e != nullptr && std::strcmp(e, "1") == 0;
+  if (e != nullptr && std::strcmp(e, "1") == 0) return true;
+  if (e != nullptr && std::strcmp(e, "0") == 0) return false;
+  return !a.causal && a.nsplit >= 0 &&
+         static_cast<long long>(a.Hq) * (a.Sq / 256) >= 2LL * sms;
 }
 
 // Visible KV tiles of the 128-row query tile at local row q0, as ranges of
@@ -140,11 +150,11 @@ std::vector<std::pair<int, int>> flash_visible_ranges(const FlashArgs& a, int q0
 FlashPlan flash_plan(const FlashArgs& a) {
   if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
   FlashPlan pl{};
+  const int sms = a.sms > 0 ? a.sms : flash_sm_count();
   // bf16 may use the two-query-tile kernel when the rows split into 256-row units
-  pl.rows_per_unit = (a.prec == Prec::kBF16 && a.Sq % 256 == 0 && two_tile_enabled()) ? 256 : 128;
+  pl.rows_per_unit = use_two_tile(a, sms) ? 256 : 128;
   pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
   const int tiles = tiles_of(a);
-  const int sms = a.sms > 0 ? a.sms : flash_sm_count();
   // per-item overhead in tiles: ~6 of the fp32 kernel's 64-key tiles, ~3 of 128-key bf16 tiles
   const int overhead = a.prec == Prec::kF32x3 ? 6 : 3;
   // the balanced schedule needs equal-cost tiles (no causal mask) and 128-row units

@@ -58,7 +58,8 @@ def test_visible_ranges_match_bruteforce(C, prec, zigzag, world, rank, blk_offse
             (q0, ranges)
 
 
-def test_plan_headline_is_balanced(C):
+def test_plan_headline_is_balanced(C, monkeypatch):
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
     # 16384 tokens x 1 head: 128 query tiles would leave 20 of 148 SMs idle
     pl = C.flash_plan_info(F32, 16384, 16384, 1, 1, 1, 64, sms=148)
     assert pl["balanced"] == 1 and pl["grid"] == 148 and pl["n_items"] == 148
@@ -70,13 +71,27 @@ def test_plan_headline_is_balanced(C):
     assert pl8["balanced"] == 1 and pl8["grid"] == 148
 
 
-def test_plan_many_heads_equal_split(C):
+def test_plan_many_heads_two_tile(C, monkeypatch):
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
+    # non-causal bf16 with >= two waves of 256-row units: the two-query-tile kernel
     pl = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, sms=148)
-    assert pl["balanced"] == 0 and pl["nsplit"] == 1 and pl["n_items"] == 4096
-    assert pl["grid"] == 148 and pl["workspace_bytes"] == 0
+    assert pl["rows_per_unit"] == 256 and pl["balanced"] == 0 and pl["nsplit"] == 1
+    assert pl["n_items"] == 2048 and pl["grid"] == 148 and pl["workspace_bytes"] == 0
+    # disabled: one-tile kernel, equal split
+    monkeypatch.setenv("RAB_FLASH_2Q", "0")
+    pl = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, sms=148)
+    assert pl["rows_per_unit"] == 128 and pl["nsplit"] == 1 and pl["n_items"] == 4096
+    monkeypatch.delenv("RAB_FLASH_2Q")
+    # too few 256-row units (64 < 2 waves): one-tile kernel; causal: one-tile kernel
+    assert C.flash_plan_info(BF16, 16384, 16384, 1, 1, 1, 128, sms=148)["rows_per_unit"] == 128
+    assert C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True,
+                             sms=148)["rows_per_unit"] == 128
+    # fp32 never
+    assert C.flash_plan_info(F32, 16384, 16384, 1, 32, 32, 64, sms=148)["rows_per_unit"] == 128
 
 
-def test_plan_causal_is_dynamic(C):
+def test_plan_causal_is_dynamic(C, monkeypatch):
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
     # long causal rows on one head: a split shortens the longest query tile
     pl = C.flash_plan_info(F32, 16384, 16384, 1, 1, 1, 64, causal=True, sms=148)
     assert pl["dynamic"] == 1 and pl["balanced"] == 0 and pl["nsplit"] == 2
@@ -85,7 +100,8 @@ def test_plan_causal_is_dynamic(C):
     assert pl["dynamic"] == 1 and pl["nsplit"] == 1
 
 
-def test_plan_forced_modes(C):
+def test_plan_forced_modes(C, monkeypatch):
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
     pl = C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=-1, sms=148)
     assert pl["balanced"] == 1 and pl["full_waves"] == 1  # 256 units: one whole wave first
     pl = C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=3, sms=148)
