@@ -175,7 +175,7 @@ struct FlashPlan {
   int nsplit;         // equal-split chunks per unit; 1 under the balanced schedule
   int balanced;       // 1: balanced schedule (n_items == grid == CTAs)
   int full_waves;     // balanced: whole-unit waves before the shared-out remainder
-  int dynamic;        // 1: dynamic claiming of equal-split items (causal, one-tile kernel)
+  int dynamic;        // 1: dynamic claiming of equal-split items (causal launches)
   int n_units;
   int n_items;
   int grid;

@@ -62,7 +62,7 @@ struct Cfg2 {
   static constexpr int kVTile = kKTile;
   static constexpr int kStages = D == 64 ? 4 : 2;
   static constexpr int kSmemTiles = 2 * kQTile + kStages * (kKTile + kVTile);
-  static constexpr int kNumBars = 4 * kStages + 16;
+  static constexpr int kNumBars = 4 * kStages + 10 + 2 * kItemSlots;
   static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
   static constexpr int kKSteps = D / 16;   // QK: K = head dim, 16 bf16 per MMA
   static constexpr int kPSteps = kN / 16;  // PV: K = keys
@@ -112,8 +112,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t* pv_done = bars + 4 * NS + 6;  // [2]
   uint64_t* o_final = bars + 4 * NS + 8;
   uint64_t* drain = bars + 4 * NS + 9;
+  uint64_t* item_full = bars + 4 * NS + 10;                 // [kItemSlots] work-item queue
+  uint64_t* item_empty = bars + 4 * NS + 10 + kItemSlots;  // [kItemSlots]
   __shared__ uint32_t tmem_slot;
   __shared__ int s_copy_ok;
+  __shared__ Item s_items[kItemSlots];  // causal: TMA thread -> MMA and softmax roles
 
   const uint32_t warp = warp_id();
   DeviceStatus* st = p.status;
@@ -135,6 +138,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < kItemSlots; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 1 + 8);  // the MMA thread + one lane per softmax warp
+    }
     fence_barrier_init();
   }
   if (warp == kWMma) {
@@ -158,8 +165,33 @@ __global__ void __launch_bounds__(kThreads2, 1)
       tma_prefetch_desc(&tmV);
       int g = 0, item_count = 0, ready_blocks = 1;
       bool ok = true;
-      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
-        const Item it = make_item(p, item, tiles_total);
+      for (int w = 0; ok; ++w, ++item_count) {
+        Item it;
+        if constexpr (kCausal) {
+          // take item w (claimed when p.dynamic) and publish it, or the end
+          // marker, to the MMA and softmax roles
+          const int slot = w % kItemSlots;
+          if (w >= kItemSlots) {
+            ok = mbar_wait(&item_empty[slot], ((w / kItemSlots) - 1) & 1, st, kSiteItemQueue, tmo);
+            if (!ok) break;
+          }
+          bool have;
+          if (p.dynamic) {
+            have = claim_item(p, tiles_total, &it);
+          } else {
+            const int item = blockIdx.x + w * gridDim.x;
+            have = item < p.n_items;
+            if (have) it = make_item(p, item, tiles_total);
+          }
+          if (!have) it.unit = -1;
+          s_items[slot] = it;
+          mbar_arrive(&item_full[slot]);
+          if (!have) break;
+        } else {
+          const int item = blockIdx.x + w * gridDim.x;
+          if (item >= p.n_items) break;
+          it = make_item(p, item, tiles_total);
+        }
         ok = mbar_wait(q_empty, (item_count & 1) ^ 1, st, kSiteQFull, tmo);
         if (!ok) break;
         mbar_arrive_expect_tx(q_full, 2 * C::kQTile);
@@ -243,8 +275,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
         mma_commit(&pv_done[x]);
         return true;
       };
-      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++item_count) {
-        const Item it = make_item(p, item, tiles_total);
+      for (int w = 0; ok; ++w, ++item_count) {
+        Item it;
+        if constexpr (kCausal) {
+          const int slot = w % kItemSlots;
+          ok = mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st, kSiteItemQueue, tmo);
+          if (!ok) break;
+          it = s_items[slot];
+          mbar_arrive(&item_empty[slot]);  // the item now lives in registers
+          if (it.unit < 0) break;
+        } else {
+          const int item = blockIdx.x + w * gridDim.x;
+          if (item >= p.n_items) break;
+          it = make_item(p, item, tiles_total);
+        }
         ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
         if (!ok) break;
         tc_fence_after();
@@ -292,8 +336,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const uint32_t o_col = tmem + lane_base + col_o(x);
     int g = 0, final_count = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-      const Item it = make_item(p, item, tiles_total);
+    for (int w = 0; ok; ++w) {
+      const int slot = w % kItemSlots;
+      Item it;
+      if constexpr (kCausal) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&item_full[slot], (w / kItemSlots) & 1, st,
+                                               kSiteItemQueue, tmo));
+        if (!ok) break;
+        it = s_items[slot];
+        if (it.unit < 0) break;
+      } else {
+        const int item = blockIdx.x + w * gridDim.x;
+        if (item >= p.n_items) break;
+        it = make_item(p, item, tiles_total);
+      }
       const int q0 = it.q0 + x * kM;
       const int qrow = q0 + row;
       float m_run = -INFINITY, l_run = 0.f;
@@ -381,9 +437,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       }
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
       const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
-      const bool split = p.nsplit > 1;
+      const bool split = it.store >= 0;
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
-      const size_t srow = static_cast<size_t>(item) * p.rows_per_unit + x * kM + row;
+      const size_t srow =
+          static_cast<size_t>(split ? it.store : 0) * p.rows_per_unit + x * kM + row;
       float* dst_f32 = nullptr;
       if (split)
         dst_f32 = p.split_acc + srow * D;
@@ -432,11 +489,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
         p.lse[r] = (have && l_run > 0.f) ? m_nat + logf(l_run) : -INFINITY;
       }
       tc_fence_before();
+      if constexpr (kCausal) {
+        __syncwarp();
+        if (lane_id() == 0) mbar_arrive(&item_empty[slot]);  // queue slot free again
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (kCausal && p.dynamic && threadIdx.x == 0) {
+    // every CTA has stopped claiming; the last one resets the claim counter
+    // for the next launch that uses this status block
+    __threadfence();
+    if (atomicAdd(&st->pad[1], 1u) == gridDim.x - 1) {
+      atomicExch(&st->pad[0], 0u);
+      atomicExch(&st->pad[1], 0u);
+    }
+  }
   if (warp == kWMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kCols);

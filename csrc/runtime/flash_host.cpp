@@ -91,21 +91,25 @@ std::vector<std::pair<int, int>> visible_ranges(const FlashArgs& a, int kN, int 
 
 // nsplit for a causal launch with dynamic claiming: simulate the CTAs claiming
 // items in kernel order (chunk-major, then head-major units with the last
-// query tiles first) and keep the split with the shortest makespan.  An item
-// costs its visible tiles plus `overhead`; a split adds one merge pass.
-int causal_split(const FlashArgs& a, int kN, int units, int tiles, int sms, int overhead) {
+// query tiles first) and keep the split with the shortest makespan.  A unit of
+// `rows` query rows works on every KV tile visible to its last 128-row tile,
+// once per 128-row tile; an item costs that work plus `overhead`, and a split
+// adds one merge pass.
+int causal_split(const FlashArgs& a, int kN, int rows, int units, int tiles, int sms,
+                 int overhead) {
   static std::mutex mu;
   static std::map<std::vector<long long>, int> cache;
-  const std::vector<long long> key{a.Sq, a.Skv,  a.nblk,       a.Hq,     a.world, a.rank,
-                                   a.blk_offset, a.zigzag, kN, sms,    overhead};
+  const std::vector<long long> key{a.Sq, a.Skv,   a.nblk, a.Hq,  a.world,  a.rank,
+                                   a.blk_offset, a.zigzag, kN, rows, sms, overhead};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  const int per_head = a.Sq / 128;
+  const int per_head = a.Sq / rows;
+  const int weight = rows / 128;
   std::vector<std::vector<std::pair<int, int>>> vis(per_head);
-  for (int qt = 0; qt < per_head; ++qt) vis[qt] = visible_ranges(a, kN, qt * 128);
+  for (int qt = 0; qt < per_head; ++qt) vis[qt] = visible_ranges(a, kN, qt * rows + rows - 128);
   int best = 1;
   double best_span = 1e300;
   for (int ns = 1; ns <= 16 && ns <= tiles; ++ns) {
@@ -121,7 +125,7 @@ int causal_split(const FlashArgs& a, int kN, int units, int tiles, int sms, int 
         const int qt = per_head - 1 - u % per_head;  // the kernel's unit order
         int n = 0;
         for (const auto& r : vis[qt]) n += std::max(0, std::min(r.second, ve) - std::max(r.first, vb));
-        const double t = load.top() + n + overhead;
+        const double t = load.top() + static_cast<double>(weight) * n + overhead;
         load.pop();
         load.push(t);
         span = std::max(span, t);
@@ -174,11 +178,12 @@ FlashPlan flash_plan(const FlashArgs& a) {
     pl.workspace_bytes = static_cast<size_t>(2 * pl.grid) * 128 * (a.D + 2) * sizeof(float);
     return pl;
   }
-  const bool dyn = a.causal && pl.rows_per_unit == 128 && dynamic_enabled();
+  const bool dyn = a.causal && dynamic_enabled();
   if (a.nsplit > 0)
     pl.nsplit = a.nsplit;
   else if (dyn)
-    pl.nsplit = causal_split(a, a.prec == Prec::kF32x3 ? 64 : 128, pl.n_units, tiles, sms, overhead);
+    pl.nsplit = causal_split(a, a.prec == Prec::kF32x3 ? 64 : 128, pl.rows_per_unit, pl.n_units,
+                             tiles, sms, overhead);
   else
     pl.nsplit = flash_choose_split(pl.n_units, tiles, sms, overhead);
   if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;
@@ -188,8 +193,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.workspace_bytes = pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * pl.rows_per_unit *
                                            (a.D + 2) * sizeof(float)
                                      : 0;
-  // causal items differ in cost: claim them dynamically (the two-tile kernel keeps its
-  // static order)
+  // causal items differ in cost: claim them dynamically
   pl.dynamic = dyn ? 1 : 0;
   return pl;
 }
