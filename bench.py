@@ -114,6 +114,9 @@ def main() -> int:
         return 2
     dev = torch.device("cuda", rt.device)
     dtype = attn.dtype
+    # before any pinned host buffer exists: keep host<->device copies on the GPU's socket
+    from ring_attention_benchmark_b200.utils.affinity import bind_to_gpu
+    host_affinity = bind_to_gpu(rt.device)
     x = inputs.normal_inputs(rank, seq, heads, head_dim, heads_kv=heads_kv,
                              seed=None if seed is None else seed + rank, mult=mult)
     q = x.q.to(dev, dtype).contiguous()
@@ -263,6 +266,7 @@ def main() -> int:
                 "data_init": (f"iid N(0,1) x {mult}, seed={'rank' if seed is None else f'{seed}+rank'}, "
                               f"scale 1/sqrt({head_dim})"),
                 "l2": "256 MiB buffer written between timed steps (outside the events)",
+                "host_affinity": host_affinity,
                 "flops_per_step_total": flops_total,
                 "wall_ms_bracketed_loop": round(wall_ms, 3),
                 "nsplit": nsplit,
