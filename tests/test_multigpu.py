@@ -19,10 +19,10 @@ def _ngpus():
     return torch.cuda.device_count()
 
 
-def _run(np, *args, timeout=240):
+def _run(np, *args, timeout=240, extra_env=None):
     if _ngpus() < np:
         pytest.skip(f"needs {np} GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", RAB_TIMEOUT_S="20")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", RAB_TIMEOUT_S="20", **(extra_env or {}))
     cmd = [sys.executable, "-m", "ring_attention_benchmark_b200.launch", "-np", str(np),
            "--timeout", str(timeout), sys.executable, WORKER] + [str(a) for a in args]
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True,
@@ -38,6 +38,14 @@ def test_fused_fp32_two_ranks(mode):
 
 def test_fused_bf16_causal_gqa_two_ranks():
     _run(2, "fused", "bf16", 1, 8, 2, 128, 1024, "direct")
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_fused_bf16_two_tile_two_ranks(causal):
+    """The two-query-tile kernel (forced; by default it serves large non-causal
+    bf16 launches) inside the fused ring, with its copy warps on the reduced
+    register budget; causal also exercises its dynamic claiming."""
+    _run(2, "fused", "bf16", causal, 8, 2, 128, 1024, "direct", extra_env={"RAB_FLASH_2Q": "1"})
 
 
 def test_comm_backends_two_ranks():
