@@ -49,6 +49,8 @@ PRESETS = {
     "ref-fp32": (16384, 1, 1, 64, "fp32", False, 1.0, None),
     # multi-head bf16, causal with zigzag sharding
     "mha-bf16-causal": (16384, 32, 32, 128, "bf16", True, 1.0, None),
+    # the same shape without a mask
+    "mha-bf16": (16384, 32, 32, 128, "bf16", False, 1.0, None),
     # long-context GQA layer shape: 32 q / 8 kv heads, causal zigzag, N(0,1)*0.5 seed 1234
     "gqa-bf16-long": (65536, 32, 8, 128, "bf16", True, 0.5, 1234),
 }
