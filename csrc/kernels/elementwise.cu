@@ -15,6 +15,8 @@
 #include <cstdint>
 #include <stdexcept>
 
+#include "flash.h"
+
 namespace rab {
 
 namespace {
@@ -134,7 +136,8 @@ __global__ void split_tf32_kernel(const float4* __restrict__ in, float4* __restr
 
 int grid_for(size_t n, int block) {
   size_t g = (n + block - 1) / block;
-  if (g > 148 * 16) g = 148 * 16;
+  const size_t cap = 16 * static_cast<size_t>(flash_sm_count());
+  if (g > cap) g = cap;
   if (g < 1) g = 1;
   return static_cast<int>(g);
 }

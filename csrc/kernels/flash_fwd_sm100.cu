@@ -862,14 +862,19 @@ int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool coop
 }  // namespace
 
 int flash_sm_count() {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
+  // per device (a process may drive GPUs of different sizes, or MIG slices)
+  static int cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+      sms = 148;  // B200 (query failed)
+    cache[dev] = sms;
   }
-  return sms;
+  return cache[dev];
 }
 
 size_t ring_v_offset(Prec prec, int Skv, int Hkv, int D) {
@@ -1007,7 +1012,7 @@ int ring_format_launch(Prec prec, const void* k, const void* v, void* k_dst, voi
   if (Skv % 32 != 0 || D % 32 != 0) throw std::runtime_error("ring_format: Skv, D % 32");
   const size_t n4 = e / 4;
   const long long n_vt = static_cast<long long>(Skv / 32) * (D / 32) * Hkv;
-  const long long n_k = std::min<long long>((n4 + 255) / 256, 148 * 8);
+  const long long n_k = std::min<long long>((n4 + 255) / 256, 8LL * flash_sm_count());
   if (n_vt + n_k > 0x7fffffffLL) throw std::runtime_error("ring_format: block too large");
   float* kb = static_cast<float*>(k_dst);
   ring_format_f32_kernel<<<static_cast<unsigned>(n_vt + n_k), dim3(32, 8), 0, stream>>>(

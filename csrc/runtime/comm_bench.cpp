@@ -23,11 +23,12 @@
 
 #include <chrono>
 #include <cstring>
-#include "strfmt.h"
 #include <stdexcept>
 #include <vector>
 
 #include "drivers.h"
+#include "flash.h"
+#include "strfmt.h"
 
 namespace rab {
 
@@ -107,7 +108,8 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   cuda_check(cudaEventCreate(&ev0), "event");
   cuda_check(cudaEventCreate(&ev1), "event");
   cuda_check(cudaEventCreate(&done), "event");
-  const int slices = o.slices > 0 ? std::min(o.slices, static_cast<int>(kMaxSlices)) : 148;
+  // default: one CTA per SM
+  const int slices = std::min(o.slices > 0 ? o.slices : flash_sm_count(), static_cast<int>(kMaxSlices));
 
   RingCopyParams rp;
   std::memset(&rp, 0, sizeof(rp));
