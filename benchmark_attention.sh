@@ -5,7 +5,8 @@
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
 # SRUN_MPI_TYPE SRUN_EXTRA_ARGS, plus RAB_DATA (normal | ref_compat), RAB_PREC (fp32 |
 # bf16), RAB_KERNEL (tcgen05 | simt), RAB_RING_MODE (direct | chain).  SIZES
-# overrides ATTENTION_SIZES.  Stops at the first
+# overrides ATTENTION_SIZES; SIZE_UNIT=elements reads the sizes as fp32 element counts
+# (default bytes).  Stops at the first
 # failing backend/size, like the reference wrapper.
 set -euo pipefail
 
@@ -15,7 +16,7 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS \
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS SIZE_UNIT \
   LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS \
   RAB_DATA RAB_PREC RAB_KERNEL RAB_RING_MODE
 configure_runtime_env
@@ -41,7 +42,7 @@ echo "========== Ring Attention Benchmark =========="
 echo "Date: $(date)"
 echo "Hostname: $(hostname)"
 echo "launcher=${LAUNCHER} np=${NP} warmup=${WARMUP} iters=${ITERS}"
-echo "sizes=${SIZES}"
+echo "sizes=${SIZES} (${SIZE_UNIT:-bytes})"
 echo "attention_backends=${ATTENTION_BACKENDS}"
 echo ""
 
@@ -54,9 +55,10 @@ for backend in ${ATTENTION_BACKENDS}; do
   fi
   echo "===== backend=${backend} ====="
   for size in ${SIZES}; do
-    echo "--- kv_size=${size} bytes ---"
-    if ! launch_ranks "${NP}" "${exe}" "${size}" "${WARMUP}" "${ITERS}"; then
-      echo "ERROR: ${backend} failed with kv_size=${size}"
+    bytes=$(size_to_bytes "${size}")
+    echo "--- kv_size=${bytes} bytes ---"
+    if ! launch_ranks "${NP}" "${exe}" "${bytes}" "${WARMUP}" "${ITERS}"; then
+      echo "ERROR: ${backend} failed with kv_size=${bytes}"
       exit 1
     fi
   done

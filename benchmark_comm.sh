@@ -3,7 +3,8 @@
 #
 # Env / benchmark.env keys: NP WARMUP ITERS SIZES COMM_SIZES BACKENDS LAUNCHER
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
-# SRUN_MPI_TYPE SRUN_EXTRA_ARGS.  SIZES overrides COMM_SIZES.  Stops at the first
+# SRUN_MPI_TYPE SRUN_EXTRA_ARGS.  SIZES overrides COMM_SIZES; SIZE_UNIT=elements reads
+# the sizes as fp32 element counts (default bytes).  Stops at the first
 # failing backend/size, like the reference wrapper.
 set -euo pipefail
 
@@ -13,7 +14,7 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS \
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS SIZE_UNIT \
   LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
 configure_runtime_env
 
@@ -37,7 +38,7 @@ echo "========== Communication (Loop) Benchmark =========="
 echo "Date: $(date)"
 echo "Hostname: $(hostname)"
 echo "launcher=${LAUNCHER} np=${NP} warmup=${WARMUP} iters=${ITERS}"
-echo "sizes=${SIZES}"
+echo "sizes=${SIZES} (${SIZE_UNIT:-bytes})"
 echo "backends=${BACKENDS}"
 echo ""
 
@@ -50,9 +51,10 @@ for backend in ${BACKENDS}; do
   fi
   echo "===== backend=${backend} ====="
   for size in ${SIZES}; do
-    echo "--- kv_size=${size} bytes ---"
-    if ! launch_ranks "${NP}" "${exe}" "${size}" "${WARMUP}" "${ITERS}"; then
-      echo "ERROR: ${backend} failed with kv_size=${size}"
+    bytes=$(size_to_bytes "${size}")
+    echo "--- kv_size=${bytes} bytes ---"
+    if ! launch_ranks "${NP}" "${exe}" "${bytes}" "${WARMUP}" "${ITERS}"; then
+      echo "ERROR: ${backend} failed with kv_size=${bytes}"
       exit 1
     fi
   done

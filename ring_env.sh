@@ -98,6 +98,18 @@ source_config_preserving_env() {
   done
 }
 
+# size_to_bytes SIZE: the programs take a shard size in bytes, as the
+# reference's do; with SIZE_UNIT=elements the configured sizes count fp32
+# elements instead (the benchmark configs quote them that way), so each is
+# multiplied by 4.
+size_to_bytes() {
+  case "${SIZE_UNIT:-bytes}" in
+    bytes) echo "$1" ;;
+    elements) echo $(( $1 * 4 )) ;;
+    *) echo "ERROR: SIZE_UNIT must be bytes or elements (got ${SIZE_UNIT})" >&2; return 1 ;;
+  esac
+}
+
 # launch_ranks NP exe args...  (LAUNCHER = local | torchrun | mpirun | srun | none)
 launch_ranks() {
   local np="$1"

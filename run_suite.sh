@@ -13,7 +13,7 @@ CONFIG=${CONFIG:-benchmark.env}
 source_config_preserving_env "${CONFIG}" \
   CONFIG RUN_LABEL RESULTS_ROOT NP_LIST RUN_TYPES WARMUP ITERS BACKENDS ATTENTION_BACKENDS \
   COMM_SIZES ATTENTION_SIZES BUILD COLLECT_ENV LAUNCHER HOSTFILE MPIRUN MPIRUN_EXTRA_ARGS \
-  SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS RAB_DATA RAB_PREC
+  SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS RAB_DATA RAB_PREC SIZE_UNIT
 configure_runtime_env
 
 RUN_LABEL=${RUN_LABEL:-"$(hostname)_$(date +%Y%m%d_%H%M%S)"}
@@ -51,6 +51,7 @@ backends=${BACKENDS}
 attention_backends=${ATTENTION_BACKENDS}
 comm_sizes=${COMM_SIZES}
 attention_sizes=${ATTENTION_SIZES}
+size_unit=${SIZE_UNIT:-bytes}
 build=${BUILD}
 collect_env=${COLLECT_ENV}
 launcher=${LAUNCHER}
@@ -71,6 +72,7 @@ BACKENDS="${BACKENDS}"
 ATTENTION_BACKENDS="${ATTENTION_BACKENDS}"
 COMM_SIZES="${COMM_SIZES}"
 ATTENTION_SIZES="${ATTENTION_SIZES}"
+SIZE_UNIT="${SIZE_UNIT:-bytes}"
 CTX
 }
 

@@ -96,6 +96,23 @@ def test_env_overrides_config_in_shell(tmp_path):
     assert r.stdout.split() == ["2", "9"]
 
 
+def test_size_unit_conversion():
+    """SIZE_UNIT=elements turns configured fp32 element counts into the byte
+    sizes the programs take; bytes (the default) passes them through."""
+    def conv(unit, size):
+        env = dict(os.environ)
+        env.pop("SIZE_UNIT", None)
+        if unit is not None:
+            env["SIZE_UNIT"] = unit
+        return subprocess.run(["bash", "-c", f"source ./ring_env.sh && size_to_bytes {size}"],
+                              cwd=ROOT, env=env, capture_output=True, text=True)
+    assert conv(None, 262144).stdout.strip() == "262144"
+    assert conv("bytes", 1048576).stdout.strip() == "1048576"
+    assert conv("elements", 262144).stdout.strip() == "1048576"
+    bad = conv("words", 16)
+    assert bad.returncode != 0 and "SIZE_UNIT" in bad.stderr
+
+
 def test_wrappers_refuse_inside_a_launched_rank():
     env = dict(os.environ, OMPI_COMM_WORLD_RANK="0")
     r = subprocess.run([os.path.join(ROOT, "benchmark_comm.sh")], env=env, capture_output=True,
