@@ -36,6 +36,7 @@
 #include <vector>
 
 #include "drivers.h"
+#include "trace.h"
 #include "launchers.h"
 
 namespace rab {
@@ -278,6 +279,7 @@ struct AttnBench::Impl {
     cudaStream_t cs = ctx.compute_stream(), ms = ctx.comm_stream();
     std::map<std::string, double> sum;
     for (int it = 0; it < o.warmup + o.iters; ++it) {
+      TraceRange range(it < o.warmup ? "rab.attn_warmup" : "rab.attn_iter");
       reset_iteration();
       double t_d2h = 0, t_mpi = 0, t_h2d = 0, t_nccl = 0, t_ca = 0, t_attn = 0, t_merge = 0,
              t_final = 0, t_prep = 0;

@@ -29,6 +29,7 @@
 #include "drivers.h"
 #include "flash.h"
 #include "strfmt.h"
+#include "trace.h"
 
 namespace rab {
 
@@ -209,6 +210,7 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
   // ---- timed repetitions ----
   double sum[6] = {0, 0, 0, 0, 0, 0};  // d2h, mpi, h2d, total, p2p(kernel), spare
   for (int rep = 0; rep < o.warmup + o.iters; ++rep) {
+    TraceRange range(rep < o.warmup ? "rab.comm_warmup" : "rab.comm_rep");
     cuda_check(cudaMemcpy(d1, h_init.data(), o.bytes, cudaMemcpyHostToDevice), "H2D reset");
     cuda_check(cudaMemset(d2, 0, o.bytes), "memset");
     cuda_check(cudaDeviceSynchronize(), "reset sync");

@@ -1,8 +1,9 @@
 // fused_ring.cpp - host side of the `b200_fused` ring attention engine.
-#include "strfmt.h"
 #include <stdexcept>
 
 #include "drivers.h"
+#include "strfmt.h"
+#include "trace.h"
 
 namespace rab {
 
@@ -68,6 +69,7 @@ uint8_t* FusedRing::slot0_v() const {
 
 void FusedRing::prepare(const void* k, const void* v, cudaStream_t stream) {
   if (k == slot0_k() && v == slot0_v() && args_.prec == Prec::kBF16) return;
+  TraceRange range("rab.ring_format");
   const int err = ring_format_launch(args_.prec, k, v, slot0_k(), slot0_v(), args_.Skv, args_.Hkv,
                                      args_.D, stream);
   cuda_check(static_cast<cudaError_t>(err), "ring_format");
@@ -75,6 +77,7 @@ void FusedRing::prepare(const void* k, const void* v, cudaStream_t stream) {
 
 void FusedRing::attend(const void* q, void* out, bool out_bf16, float* lse, float scale,
                        cudaStream_t stream) {
+  TraceRange range("rab.fused_attention");
   FlashArgs a = args_;
   a.q = q;
   a.out = out;
