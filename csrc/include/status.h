@@ -39,6 +39,13 @@ enum WaitSite : uint32_t {
   kSiteItemQueue = 16,     // flash kernel's in-CTA work-item queue
 };
 
+// Sites of the RAB_DEBUG_BOUNDS index checks (reported as `where` with kStatusBounds).
+enum BoundsSite : uint32_t {
+  kBoundsQRow = 101,       // query row of a work item (Q load, output write)
+  kBoundsRecord = 102,     // split partial record written by a work item
+  kBoundsMergeRecord = 103,  // split partial record read by a merge kernel
+};
+
 struct DeviceStatus {
   uint32_t code;       // StatusCode, first error wins
   uint32_t where;      // WaitSite of the first error
@@ -72,6 +79,21 @@ __device__ __forceinline__ void st_record(DeviceStatus* st, uint32_t code, uint3
 __device__ __forceinline__ void st_record_timeout(DeviceStatus* st, uint32_t where,
                                                   uint32_t detail = 0) {
   st_record(st, kStatusTimeout, where, detail);
+}
+
+// Index check of a computed global access.  Builds with RAB_DEBUG_BOUNDS
+// evaluate `ok`; when it is false they record kStatusBounds (`where` = the
+// BoundsSite, `detail` = the offending index) and return false so the caller
+// skips the access.  Default builds compile the check to `true`.
+__device__ __forceinline__ bool st_bounds(DeviceStatus* st, bool ok, uint32_t where,
+                                          uint32_t detail) {
+#ifdef RAB_DEBUG_BOUNDS
+  if (!ok) st_record(st, kStatusBounds, where, detail);
+  return ok;
+#else
+  (void)st, (void)ok, (void)where, (void)detail;
+  return true;
+#endif
 }
 #endif
 

@@ -438,6 +438,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
       const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
       const bool split = it.store >= 0;
+      // (RAB_DEBUG_BOUNDS builds: an out-of-range row or record is reported, its stores skipped)
+      const bool out_in =
+          st_bounds(st, qrow < p.Sq && it.h < p.Hq && (!split || it.store < p.n_items),
+                    split ? kBoundsRecord : kBoundsQRow, split ? it.store : qrow);
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
       const size_t srow =
           static_cast<size_t>(split ? it.store : 0) * p.rows_per_unit + x * kM + row;
@@ -458,7 +462,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        if (dst_f32 != nullptr) {
+        if (!out_in) {
+          // nothing stored (the TMEM load above is warp-collective and stays)
+        } else if (dst_f32 != nullptr) {
           float4* d4 = reinterpret_cast<float4*>(dst_f32 + c);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
@@ -479,7 +485,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
                                            __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
-      if (split) {
+      if (!out_in) {
+        // reported above
+      } else if (split) {
         p.split_m[srow] = m_nat;
         p.split_l[srow] = l_run;
       } else if (p.partial) {

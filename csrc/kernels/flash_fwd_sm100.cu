@@ -414,12 +414,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         it = work_item(p, w, tiles_total, s_work);
       }
       const int qrow = it.q0 + row;
+      // (RAB_DEBUG_BOUNDS builds: an out-of-range row is reported and row 0 read instead)
+      const bool q_in = st_bounds(st, qrow < p.Sq && it.h < p.Hq, kBoundsQRow, qrow);
+      const size_t q_off = q_in ? (static_cast<size_t>(qrow) * p.Hq + it.h) * D : 0;
       // ---- this warpgroup's half of the Q row -> TMEM ----
       {
         if constexpr (C::kTF32) {
           const float4* qp = reinterpret_cast<const float4*>(
-              static_cast<const float*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D +
-              half * kHalfD);
+              static_cast<const float*>(p.q) + q_off + half * kHalfD);
           uint32_t big[32], small[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -434,8 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           constexpr int kQc = D / 4;  // packed bf16 columns per warpgroup
           const uint4* qp = reinterpret_cast<const uint4*>(
-              static_cast<const uint16_t*>(p.q) + (static_cast<size_t>(qrow) * p.Hq + it.h) * D +
-              half * kHalfD);
+              static_cast<const uint16_t*>(p.q) + q_off + half * kHalfD);
           uint32_t w[32];
 #pragma unroll
           for (int i = 0; i < kQc / 4; ++i) {
@@ -580,6 +581,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item ie = kCausal ? s_items[slot] : work_item(p, w, tiles_total, s_work);
       const size_t r = static_cast<size_t>(ie.q0 + row) * p.Hq + ie.h;
       const bool split = ie.store >= 0;
+      // (RAB_DEBUG_BOUNDS builds: an out-of-range row or record is reported, its stores skipped)
+      const bool out_in = st_bounds(
+          st, ie.q0 + row < p.Sq && ie.h < p.Hq &&
+                  (!split || ie.store < (p.balanced ? 2 * p.n_items : p.n_items)),
+          split ? kBoundsRecord : kBoundsQRow, split ? ie.store : ie.q0 + row);
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
       float* dst_f32 = nullptr;
       if (split)
@@ -598,7 +604,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        if (dst_f32 != nullptr) {
+        if (!out_in) {
+          // nothing stored (the TMEM load above is warp-collective and stays)
+        } else if (dst_f32 != nullptr) {
           float4* d4 = reinterpret_cast<float4*>(dst_f32 + c);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
@@ -620,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
-      if (half == 0) {
+      if (half == 0 && out_in) {
         if (split) {
           p.split_m[static_cast<size_t>(ie.store) * kM + row] = m_nat;
           p.split_l[static_cast<size_t>(ie.store) * kM + row] = l_run;
@@ -665,6 +673,7 @@ __device__ __forceinline__ void write_merged(const FlashParams& p, int unit, int
                                              float mx, float l, float4 a) {
   const int h = unit_head(p, unit);
   const int qrow = unit_q0(p, unit) + row;
+  if (!st_bounds(p.status, qrow < p.Sq && h < p.Hq, kBoundsQRow, qrow)) return;
   const size_t r = static_cast<size_t>(qrow) * p.Hq + h;
   if (p.partial) {
     reinterpret_cast<float4*>(p.acc + r * D)[c] = a;
@@ -695,6 +704,8 @@ __device__ __forceinline__ void write_merged(const FlashParams& p, int unit, int
 template <int D>
 __device__ __forceinline__ void add_record(const FlashParams& p, size_t rec, int R, int row, int c,
                                            float mref, float& l, float4& a) {
+  const size_t n_rec = p.balanced ? 2 * static_cast<size_t>(p.n_items) : p.n_items;
+  if (!st_bounds(p.status, rec < n_rec, kBoundsMergeRecord, static_cast<uint32_t>(rec))) return;
   const float mk = p.split_m[rec * R + row];
   const float w = (mk == -INFINITY) ? 0.f : expf(mk - mref);
   l += w * p.split_l[rec * R + row];

@@ -37,6 +37,10 @@ NVCC_FLAGS = ARCH + [
 ]
 if os.environ.get("RAB_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
+# RAB_DEBUG_BOUNDS=1: index checks in the flash kernels that report through the
+# device status word instead of faulting (see csrc/include/status.h)
+if os.environ.get("RAB_DEBUG_BOUNDS") == "1":
+    NVCC_FLAGS.append("-DRAB_DEBUG_BOUNDS")
 CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG"]
 
 sources = sorted(
