@@ -6,7 +6,8 @@
 # SRUN_MPI_TYPE SRUN_EXTRA_ARGS, plus RAB_DATA (normal | ref_compat), RAB_PREC (fp32 |
 # bf16), RAB_KERNEL (tcgen05 | simt), RAB_RING_MODE (direct | chain).  SIZES
 # overrides ATTENTION_SIZES; SIZE_UNIT=elements reads the sizes as fp32 element counts
-# (default bytes).  Stops at the first
+# (default bytes).  RESUME=1 with
+# RAB_RESULTS_JSONL skips configurations that file already records.  Stops at the first
 # failing backend/size, like the reference wrapper.
 set -euo pipefail
 
@@ -16,7 +17,7 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS SIZE_UNIT \
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS SIZE_UNIT RESUME RAB_RESULTS_JSONL \
   LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS \
   RAB_DATA RAB_PREC RAB_KERNEL RAB_RING_MODE
 configure_runtime_env
@@ -56,6 +57,13 @@ for backend in ${ATTENTION_BACKENDS}; do
   echo "===== backend=${backend} ====="
   for size in ${SIZES}; do
     bytes=$(size_to_bytes "${size}")
+    if [[ "${RESUME:-0}" == "1" && -n "${RAB_RESULTS_JSONL:-}" ]] &&
+      "${RAB_PYTHON}" -m ring_attention_benchmark_b200.utils.results has --kind attention \
+        --backend "${backend}" --bytes "${bytes}" --ranks "${NP}" --warmup "${WARMUP}" \
+        --iters "${ITERS}" --prec "${RAB_PREC:-fp32}" --data "${RAB_DATA:-normal}"; then
+      echo "SKIP backend=${backend} kv_size=${bytes} (already recorded in ${RAB_RESULTS_JSONL})"
+      continue
+    fi
     echo "--- kv_size=${bytes} bytes ---"
     if ! launch_ranks "${NP}" "${exe}" "${bytes}" "${WARMUP}" "${ITERS}"; then
       echo "ERROR: ${backend} failed with kv_size=${bytes}"

@@ -4,7 +4,8 @@
 # Env / benchmark.env keys: NP WARMUP ITERS SIZES COMM_SIZES BACKENDS LAUNCHER
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
 # SRUN_MPI_TYPE SRUN_EXTRA_ARGS.  SIZES overrides COMM_SIZES; SIZE_UNIT=elements reads
-# the sizes as fp32 element counts (default bytes).  Stops at the first
+# the sizes as fp32 element counts (default bytes).  RESUME=1 with
+# RAB_RESULTS_JSONL skips configurations that file already records.  Stops at the first
 # failing backend/size, like the reference wrapper.
 set -euo pipefail
 
@@ -14,7 +15,7 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS SIZE_UNIT \
+source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS SIZE_UNIT RESUME RAB_RESULTS_JSONL \
   LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
 configure_runtime_env
 
@@ -52,6 +53,13 @@ for backend in ${BACKENDS}; do
   echo "===== backend=${backend} ====="
   for size in ${SIZES}; do
     bytes=$(size_to_bytes "${size}")
+    if [[ "${RESUME:-0}" == "1" && -n "${RAB_RESULTS_JSONL:-}" ]] &&
+      "${RAB_PYTHON}" -m ring_attention_benchmark_b200.utils.results has --kind comm \
+        --backend "${backend}" --bytes "${bytes}" --ranks "${NP}" --warmup "${WARMUP}" \
+        --iters "${ITERS}"; then
+      echo "SKIP backend=${backend} kv_size=${bytes} (already recorded in ${RAB_RESULTS_JSONL})"
+      continue
+    fi
     echo "--- kv_size=${bytes} bytes ---"
     if ! launch_ranks "${NP}" "${exe}" "${bytes}" "${WARMUP}" "${ITERS}"; then
       echo "ERROR: ${backend} failed with kv_size=${bytes}"

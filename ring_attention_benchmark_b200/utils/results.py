@@ -113,3 +113,49 @@ def append_jsonl(record: Dict) -> None:
     rec.setdefault("time", time.time())
     with open(path, "a") as f:
         f.write(json.dumps(rec, sort_keys=True) + "\n")
+
+
+def has_record(path: str, **match) -> bool:
+    """True when the JSONL file holds a record whose fields equal `match`
+    (a resumed sweep skips such configurations).  Unreadable lines are ignored."""
+    if not path or not os.path.exists(path):
+        return False
+    with open(path) as f:
+        for line in f:
+            try:
+                rec = json.loads(line)
+            except ValueError:
+                continue
+            if all(rec.get(k) == v for k, v in match.items()):
+                return True
+    return False
+
+
+def main(argv=None) -> int:
+    """``python -m ring_attention_benchmark_b200.utils.results has --kind comm
+    --backend B --bytes N --ranks R --warmup W --iters I [--prec P --data D]``:
+    exit 0 when $RAB_RESULTS_JSONL already records that configuration, 1 when
+    not (used by the wrappers' RESUME=1)."""
+    import argparse
+
+    ap = argparse.ArgumentParser(prog="results")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    h = sub.add_parser("has")
+    h.add_argument("--kind", required=True, choices=("comm", "attention"))
+    h.add_argument("--backend", required=True)
+    for k in ("bytes", "ranks", "warmup", "iters"):
+        h.add_argument("--" + k, type=int, required=True)
+    h.add_argument("--prec")
+    h.add_argument("--data")
+    a = ap.parse_args(argv)
+    match = {"kind": a.kind, "backend": a.backend, "bytes": a.bytes, "ranks": a.ranks,
+             "warmup": a.warmup, "iters": a.iters}
+    if a.prec:
+        match["prec"] = a.prec
+    if a.data:
+        match["data"] = a.data
+    return 0 if has_record(os.environ.get("RAB_RESULTS_JSONL", ""), **match) else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -77,7 +77,8 @@ CTX
 }
 
 write_launch_examples() {
-  local prefix="env CONFIG=\"${CONFIG_PATH}\" RUN_LABEL=\"${RUN_LABEL}\" RESULTS_ROOT=\"${RESULTS_ROOT}\""
+  # results go to the run directory's JSONL file; RESUME=1 makes a rerun skip what it records
+  local prefix="env CONFIG=\"${CONFIG_PATH}\" RUN_LABEL=\"${RUN_LABEL}\" RESULTS_ROOT=\"${RESULTS_ROOT}\" RAB_RESULTS_JSONL=\"${RUN_DIR}/results.jsonl\""
   {
     echo "# Ring attention benchmark launch examples"
     echo "# Preparation already created: ${RUN_DIR}"

@@ -2,6 +2,7 @@
 grammar (label quirks included), config precedence (environment over file,
 SIZES over the per-family lists), the correctness checker's PASS rule and its
 oracle mode, and the shell scripts."""
+import json
 import os
 import re
 import subprocess
@@ -148,3 +149,27 @@ def test_cli_argument_validation():
     assert cli.comm_main("nccl", ["6"]) == 1       # not a multiple of 4
     assert cli.attention_main("nccl", ["300"]) == 1  # not a multiple of 256
     assert cli.comm_main("nope", ["4"]) == 1
+
+
+def test_resume_skips_recorded_configurations(tmp_path):
+    """RESUME=1: a configuration already in RAB_RESULTS_JSONL is skipped without
+    launching any rank; an unrecorded one is not."""
+    from ring_attention_benchmark_b200.utils import results
+
+    jl = tmp_path / "r.jsonl"
+    rec = {"kind": "comm", "backend": "staged", "bytes": 4096, "ranks": 2, "warmup": 1,
+           "iters": 2, "avg_ms": {}}
+    jl.write_text(json.dumps(rec) + "\nnot json\n")
+    assert results.has_record(str(jl), kind="comm", backend="staged", bytes=4096, ranks=2,
+                              warmup=1, iters=2)
+    assert not results.has_record(str(jl), kind="comm", backend="staged", bytes=8192, ranks=2,
+                                  warmup=1, iters=2)
+    env = dict(os.environ, RESUME="1", RAB_RESULTS_JSONL=str(jl), NP="2", WARMUP="1",
+               ITERS="2", SIZES="4096", BACKENDS="staged", LAUNCHER="none",
+               CONFIG=str(tmp_path / "none.env"))
+    for k in ("OMPI_COMM_WORLD_RANK", "PMI_RANK", "SLURM_PROCID", "RANK", "SIZE_UNIT"):
+        env.pop(k, None)
+    r = subprocess.run([os.path.join(ROOT, "benchmark_comm.sh")], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "SKIP backend=staged kv_size=4096" in r.stdout and "--- kv_size" not in r.stdout
