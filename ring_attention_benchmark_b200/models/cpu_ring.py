@@ -42,14 +42,21 @@ def merge_fp32(run, new):
     return a.unsqueeze(-1) * acc_r + b.unsqueeze(-1) * acc_n, m, a * l_r + b * l_n
 
 
+class RingDataError(RuntimeError):
+    """A block received over the ring is not finite (a corrupt or NaN shard)."""
+
+
 def ring_attention_cpu(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                        scale: Optional[float] = None,
                        q_pos: Optional[torch.Tensor] = None,
-                       pos_of_rank=None, group=None) -> torch.Tensor:
+                       pos_of_rank=None, group=None, check_finite: bool = True) -> torch.Tensor:
     """Every rank calls this with its own shard; returns its normalised output.
 
     For causal masking pass this rank's global query positions `q_pos` and
-    `pos_of_rank(r)` giving rank r's key positions.
+    `pos_of_rank(r)` giving rank r's key positions.  With `check_finite` every
+    received block is checked and a non-finite one raises `RingDataError`
+    naming the rank it came from and the step.  A peer that stops taking part
+    makes the exchange fail within the process group's timeout.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -70,6 +77,11 @@ def ring_attention_cpu(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    dist.P2POp(dist.irecv, nk, left, group), dist.P2POp(dist.irecv, nv, left, group)]
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
+            if check_finite and not (torch.isfinite(nk).all() and torch.isfinite(nv).all()):
+                origin = (rank - step - 1) % world
+                raise RingDataError(
+                    f"rank {rank}: K/V block of rank {origin} received from rank {left} at ring "
+                    f"step {step + 1} is not finite")
             cur_k, cur_v = nk, nv
     acc, _, l = state
     return acc / l.unsqueeze(-1)

@@ -15,8 +15,26 @@ from ring_attention_benchmark_b200.models import oracle  # noqa: E402
 from ring_attention_benchmark_b200.models.cpu_ring import ring_attention_cpu  # noqa: E402
 
 
+def fault(case):
+    """Injected on the host: rank 1 sends NaN K/V ("fault_nan") or leaves before
+    the ring ("fault_exit"); the others must fail with a clear error, fast."""
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=8))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(64, 1, 32, generator=g) for _ in range(3))
+    if rank == 1 and case == "fault_exit":
+        print("rank 1 leaves before the ring", flush=True)
+        os._exit(3)
+    if rank == 1 and case == "fault_nan":
+        k = torch.full_like(k, float("nan"))
+    ring_attention_cpu(q, k, v)
+    print(f"rank {rank} finished the ring", flush=True)
+
+
 def main():
     case = sys.argv[1]
+    if case.startswith("fault_"):
+        return fault(case)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     rank, world = dist.get_rank(), dist.get_world_size()
     g = torch.Generator().manual_seed(0)
