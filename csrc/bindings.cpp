@@ -7,6 +7,7 @@
 #include <string>
 
 #include "launchers.h"
+#include "strfmt.h"
 
 namespace rab {
 namespace {
@@ -14,19 +15,19 @@ namespace {
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 void check_cuda(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  RAB_CHECK(t.is_cuda(), "%s must be a CUDA tensor", name);
+  RAB_CHECK(t.is_contiguous(), "%s must be contiguous", name);
 }
 
 void check_launch(int err, const char* what) {
-  TORCH_CHECK(err == 0, what, " launch failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
+  RAB_CHECK(err == 0, "%s launch failed: %s", what, cudaGetErrorString(static_cast<cudaError_t>(err)));
 }
 
 DeviceStatus* status_ptr(const c10::optional<torch::Tensor>& status) {
   if (!status.has_value()) return nullptr;
   const auto& s = *status;
   check_cuda(s, "status");
-  TORCH_CHECK(s.scalar_type() == torch::kInt32 && s.numel() >= 8, "status must be int32[8]");
+  RAB_CHECK(s.scalar_type() == torch::kInt32 && s.numel() >= 8, "status must be int32[8]");
   return reinterpret_cast<DeviceStatus*>(s.data_ptr());
 }
 
@@ -36,12 +37,12 @@ void umma_selftest(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_in_
   check_cuda(B, "B");
   check_cuda(D, "D");
   const bool tf32 = A.scalar_type() == torch::kFloat32;
-  TORCH_CHECK(tf32 || A.scalar_type() == torch::kBFloat16, "A must be fp32 or bf16");
-  TORCH_CHECK(B.scalar_type() == A.scalar_type(), "A and B must share a dtype");
-  TORCH_CHECK(A.dim() == 2 && A.size(0) == 128, "A must be [128, K]");
+  RAB_CHECK(tf32 || A.scalar_type() == torch::kBFloat16, "A must be fp32 or bf16");
+  RAB_CHECK(B.scalar_type() == A.scalar_type(), "A and B must share a dtype");
+  RAB_CHECK(A.dim() == 2 && A.size(0) == 128, "A must be [128, K]");
   const int K = static_cast<int>(A.size(1));
   const int N = static_cast<int>(b_mn_major ? B.size(1) : B.size(0));
-  TORCH_CHECK(D.scalar_type() == torch::kFloat32 && D.size(0) == 128 && D.size(1) == N,
+  RAB_CHECK(D.scalar_type() == torch::kFloat32 && D.size(0) == 128 && D.size(1) == N,
               "D must be fp32 [128, N]");
   const c10::cuda::CUDAGuard guard(A.device());
   check_launch(umma_selftest_launch(A.data_ptr(), B.data_ptr(), D.data_ptr<float>(), N, K, tf32,
@@ -54,9 +55,9 @@ void simt_partial_attention(torch::Tensor Q, torch::Tensor K, torch::Tensor V, t
                             double scale, int64_t causal_offset, bool normalize) {
   for (auto* p : {&Q, &K, &V, &acc}) {
     check_cuda(*p, "tensor");
-    TORCH_CHECK(p->scalar_type() == torch::kFloat32, "simt attention is fp32 only");
+    RAB_CHECK(p->scalar_type() == torch::kFloat32, "simt attention is fp32 only");
   }
-  TORCH_CHECK(Q.dim() == 3 && K.dim() == 3 && V.dim() == 3, "Q/K/V must be [seq, heads, D]");
+  RAB_CHECK(Q.dim() == 3 && K.dim() == 3 && V.dim() == 3, "Q/K/V must be [seq, heads, D]");
   const int D = static_cast<int>(Q.size(2));
   const c10::cuda::CUDAGuard guard(Q.device());
   check_launch(simt_partial_attention_launch(
@@ -74,7 +75,7 @@ void merge_lse(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_run, 
   for (auto* p : {&m_run, &l_run, &acc_run, &m_new, &l_new, &acc_new}) check_cuda(*p, "tensor");
   const int D = static_cast<int>(acc_run.size(-1));
   const int rows = static_cast<int>(m_run.numel());
-  TORCH_CHECK(acc_run.numel() == static_cast<int64_t>(rows) * D, "acc/m shape mismatch");
+  RAB_CHECK(acc_run.numel() == static_cast<int64_t>(rows) * D, "acc/m shape mismatch");
   const c10::cuda::CUDAGuard guard(m_run.device());
   check_launch(merge_lse_launch(m_run.data_ptr<float>(), l_run.data_ptr<float>(),
                                 acc_run.data_ptr<float>(), m_new.data_ptr<float>(),
@@ -89,7 +90,7 @@ void normalize(torch::Tensor acc, torch::Tensor m, torch::Tensor l, torch::Tenso
   const int D = static_cast<int>(acc.size(-1));
   const int rows = static_cast<int>(m.numel());
   const bool bf16 = out.scalar_type() == torch::kBFloat16;
-  TORCH_CHECK(bf16 || out.scalar_type() == torch::kFloat32, "out must be fp32 or bf16");
+  RAB_CHECK(bf16 || out.scalar_type() == torch::kFloat32, "out must be fp32 or bf16");
   const c10::cuda::CUDAGuard guard(acc.device());
   check_launch(normalize_launch(acc.data_ptr<float>(), m.data_ptr<float>(), l.data_ptr<float>(),
                                 out.data_ptr(), bf16, lse ? lse->data_ptr<float>() : nullptr, rows,
@@ -100,7 +101,7 @@ void normalize(torch::Tensor acc, torch::Tensor m, torch::Tensor l, torch::Tenso
 void cast(torch::Tensor in, torch::Tensor out) {
   check_cuda(in, "in");
   check_cuda(out, "out");
-  TORCH_CHECK(in.numel() == out.numel(), "cast: size mismatch");
+  RAB_CHECK(in.numel() == out.numel(), "cast: size mismatch");
   const c10::cuda::CUDAGuard guard(in.device());
   if (in.scalar_type() == torch::kFloat32 && out.scalar_type() == torch::kBFloat16) {
     check_launch(cast_f32_bf16_launch(in.data_ptr<float>(), out.data_ptr(), in.numel(),
@@ -111,16 +112,16 @@ void cast(torch::Tensor in, torch::Tensor out) {
                                       cur_stream()),
                  "cast_bf16_f32");
   } else {
-    TORCH_CHECK(false, "cast supports fp32<->bf16 only");
+    RAB_CHECK(false, "cast supports fp32<->bf16 only");
   }
 }
 
 void split_tf32(torch::Tensor in, torch::Tensor big, torch::Tensor small) {
   for (auto* p : {&in, &big, &small}) {
     check_cuda(*p, "tensor");
-    TORCH_CHECK(p->scalar_type() == torch::kFloat32, "split_tf32 is fp32 only");
+    RAB_CHECK(p->scalar_type() == torch::kFloat32, "split_tf32 is fp32 only");
   }
-  TORCH_CHECK(in.numel() == big.numel() && in.numel() == small.numel(), "split_tf32: size mismatch");
+  RAB_CHECK(in.numel() == big.numel() && in.numel() == small.numel(), "split_tf32: size mismatch");
   const c10::cuda::CUDAGuard guard(in.device());
   check_launch(split_tf32_launch(in.data_ptr<float>(), big.data_ptr<float>(),
                                  small.data_ptr<float>(), in.numel(), cur_stream()),
@@ -129,7 +130,7 @@ void split_tf32(torch::Tensor in, torch::Tensor big, torch::Tensor small) {
 
 void wait_selftest(torch::Tensor flag, int64_t target, double timeout_s, torch::Tensor status) {
   check_cuda(flag, "flag");
-  TORCH_CHECK(flag.scalar_type() == torch::kInt64 && flag.numel() >= 1, "flag must be int64");
+  RAB_CHECK(flag.scalar_type() == torch::kInt64 && flag.numel() >= 1, "flag must be int64");
   const c10::cuda::CUDAGuard guard(flag.device());
   check_launch(wait_selftest_launch(reinterpret_cast<const uint64_t*>(flag.data_ptr()),
                                     static_cast<uint64_t>(target),

@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 
 #include "flash.h"
+#include "strfmt.h"
 
 namespace rab {
 namespace {
@@ -13,26 +14,26 @@ namespace {
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 Prec to_prec(int64_t p) {
-  TORCH_CHECK(p == 0 || p == 1, "prec must be 0 (bf16) or 1 (fp32 via 3xTF32)");
+  RAB_CHECK(p == 0 || p == 1, "prec must be 0 (bf16) or 1 (fp32 via 3xTF32)");
   return static_cast<Prec>(p);
 }
 
 void ring_format(int64_t prec, torch::Tensor k, torch::Tensor v, torch::Tensor slot) {
   const Prec pr = to_prec(prec);
-  TORCH_CHECK(k.is_cuda() && v.is_cuda() && slot.is_cuda(), "CUDA tensors required");
-  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && slot.is_contiguous(), "contiguous tensors");
-  TORCH_CHECK(k.dim() == 3 && v.sizes() == k.sizes(), "k/v must be [Skv, Hkv, D]");
-  TORCH_CHECK(k.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
+  RAB_CHECK(k.is_cuda() && v.is_cuda() && slot.is_cuda(), "CUDA tensors required");
+  RAB_CHECK(k.is_contiguous() && v.is_contiguous() && slot.is_contiguous(), "contiguous tensors");
+  RAB_CHECK(k.dim() == 3 && v.sizes() == k.sizes(), "k/v must be [Skv, Hkv, D]");
+  RAB_CHECK(k.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
               "k/v dtype does not match prec");
   const int Skv = k.size(0), Hkv = k.size(1), D = k.size(2);
   const size_t need = ring_block_bytes(pr, Skv, Hkv, D);
-  TORCH_CHECK(static_cast<size_t>(slot.numel() * slot.element_size()) >= need, "slot too small");
+  RAB_CHECK(static_cast<size_t>(slot.numel() * slot.element_size()) >= need, "slot too small");
   const c10::cuda::CUDAGuard guard(k.device());
   uint8_t* base = static_cast<uint8_t*>(slot.data_ptr());
   const int err = ring_format_launch(pr, k.data_ptr(), v.data_ptr(), base,
                                      base + ring_v_offset(pr, Skv, Hkv, D), Skv, Hkv, D,
                                      cur_stream());
-  TORCH_CHECK(err == 0, "ring_format failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
+  RAB_CHECK(err == 0, "ring_format failed: %s", cudaGetErrorString(static_cast<cudaError_t>(err)));
 }
 
 std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slots, int64_t nblk,
@@ -43,10 +44,10 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
                                c10::optional<torch::Tensor> l, torch::Tensor status,
                                double timeout_s, int64_t grid) {
   const Prec pr = to_prec(prec);
-  TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.dim() == 3, "q must be contiguous [Sq, Hq, D]");
-  TORCH_CHECK(q.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
+  RAB_CHECK(q.is_cuda() && q.is_contiguous() && q.dim() == 3, "q must be contiguous [Sq, Hq, D]");
+  RAB_CHECK(q.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
               "q dtype does not match prec");
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 8,
+  RAB_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 8,
               "status must be int32[8] on the GPU");
   const c10::cuda::CUDAGuard guard(q.device());
   FlashArgs a;
@@ -60,7 +61,7 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
   a.nblk = static_cast<int>(nblk);
   a.scale = static_cast<float>(scale);
   const size_t bb = ring_block_bytes(pr, a.Skv, a.Hkv, a.D);
-  TORCH_CHECK(static_cast<size_t>(slots.numel() * slots.element_size()) >= bb * nblk,
+  RAB_CHECK(static_cast<size_t>(slots.numel() * slots.element_size()) >= bb * nblk,
               "slots tensor too small for nblk blocks");
   uint8_t* base = static_cast<uint8_t*>(slots.data_ptr());
   a.k_base = base;
@@ -80,7 +81,7 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
     a.m = m ? m->data_ptr<float>() : nullptr;
     a.l = l ? l->data_ptr<float>() : nullptr;
   } else {
-    TORCH_CHECK(out.has_value(), "out (or partial acc/m/l) is required");
+    RAB_CHECK(out.has_value(), "out (or partial acc/m/l) is required");
     a.out = out->data_ptr();
     a.out_bf16 = out->scalar_type() == torch::kBFloat16;
     a.lse = lse ? lse->data_ptr<float>() : nullptr;
@@ -94,8 +95,8 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
     a.workspace_bytes = pl.workspace_bytes;
   }
   const int err = flash_run(a, pl, cur_stream());
-  TORCH_CHECK(err == 0, "flash_fwd launch failed: ",
-              cudaGetErrorString(static_cast<cudaError_t>(err)));
+  RAB_CHECK(err == 0, "flash_fwd launch failed: %s",
+            cudaGetErrorString(static_cast<cudaError_t>(err)));
   // nsplit -1 reports the balanced schedule
   return {pl.balanced ? -1 : pl.nsplit, pl.n_items, pl.grid};
 }

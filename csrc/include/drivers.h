@@ -97,6 +97,7 @@ class FusedRing {
   uint8_t* slot0_v() const;
   int grid() const { return plan_.grid; }
   int nsplit() const { return plan_.balanced ? -1 : plan_.nsplit; }  // -1: balanced schedule
+  const FlashArgs& args() const { return args_; }  // shapes and precision of the engine
   uint64_t launches() const { return epoch_; }
 
  private:

@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <stdexcept>
 #include <string>
 
 namespace rab {
@@ -27,3 +28,11 @@ inline std::string strfmt(const char* fmt, ...) {
 }
 
 }  // namespace rab
+
+// Argument check for the Python bindings: throws std::runtime_error (a Python
+// RuntimeError through pybind11) with a printf-style message.  Used instead of
+// TORCH_CHECK, whose message builder goes through std::ostringstream.
+#define RAB_CHECK(cond, ...)                                      \
+  do {                                                            \
+    if (!(cond)) throw std::runtime_error(::rab::strfmt(__VA_ARGS__)); \
+  } while (0)

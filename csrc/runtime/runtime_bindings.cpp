@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "drivers.h"
+#include "strfmt.h"
 #include "host_comm.h"
 #include "ring_context.h"
 
@@ -26,7 +27,41 @@ Prec prec_from(const std::string& s) {
 }
 
 void check_cpu_contig(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(!t.is_cuda() && t.is_contiguous(), name, " must be a contiguous CPU tensor");
+  RAB_CHECK(!t.is_cuda() && t.is_contiguous(), "%s must be a contiguous CPU tensor", name);
+}
+
+// Inputs and outputs of a FusedRing call must match the engine's shapes and
+// precision exactly (the kernels index them with the engine's sizes) and sit
+// on one GPU.  Null pointers are skipped.
+void check_fused_io(const FusedRing& f, const torch::Tensor* q, const torch::Tensor* k,
+                    const torch::Tensor* v, const torch::Tensor* out,
+                    const c10::optional<torch::Tensor>& lse) {
+  const FlashArgs& a = f.args();
+  const auto in_type = a.prec == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32;
+  const int64_t nq = static_cast<int64_t>(a.Sq) * a.Hq * a.D;
+  const int64_t nkv = static_cast<int64_t>(a.Skv) * a.Hkv * a.D;
+  const torch::Tensor* first = q ? q : k;
+  auto check = [&](const torch::Tensor* t, const char* name, int64_t numel, bool out_tensor) {
+    if (t == nullptr) return;
+    RAB_CHECK(t->is_cuda() && t->is_contiguous(), "%s: a contiguous CUDA tensor is required", name);
+    RAB_CHECK(t->device() == first->device(), "%s: all tensors must be on one GPU", name);
+    RAB_CHECK(t->numel() == numel, "%s: expected %lld elements for the engine's shape, got %lld",
+              name, static_cast<long long>(numel), static_cast<long long>(t->numel()));
+    if (out_tensor) {
+      RAB_CHECK(t->scalar_type() == torch::kFloat32 || t->scalar_type() == torch::kBFloat16,
+                "%s: must be float32 or bfloat16", name);
+    } else {
+      RAB_CHECK(t->scalar_type() == in_type, "%s: dtype does not match the engine's precision", name);
+    }
+  };
+  check(q, "q", nq, false);
+  check(k, "k", nkv, false);
+  check(v, "v", nkv, false);
+  check(out, "out", nq, true);
+  if (lse) {
+    check(&*lse, "lse", static_cast<int64_t>(a.Sq) * a.Hq, true);
+    RAB_CHECK(lse->scalar_type() == torch::kFloat32, "lse: must be float32");
+  }
 }
 
 }  // namespace
@@ -54,7 +89,7 @@ void register_runtime(py::module_& m) {
              check_cpu_contig(send, "send");
              check_cpu_contig(recv, "recv");
              const size_t n = send.numel() * send.element_size();
-             TORCH_CHECK(static_cast<size_t>(recv.numel() * recv.element_size()) == n,
+             RAB_CHECK(static_cast<size_t>(recv.numel() * recv.element_size()) == n,
                          "send/recv size mismatch");
              py::gil_scoped_release nogil;
              h.ring_sendrecv(send.data_ptr(), recv.data_ptr(), n);
@@ -180,7 +215,7 @@ void register_runtime(py::module_& m) {
       .def("output",
            [](AttnBench& b, torch::Tensor dst) {
              check_cpu_contig(dst, "dst");
-             TORCH_CHECK(static_cast<size_t>(dst.numel() * dst.element_size()) == b.output_bytes(),
+             RAB_CHECK(static_cast<size_t>(dst.numel() * dst.element_size()) == b.output_bytes(),
                          "output size mismatch");
              b.copy_output(dst.data_ptr());
            })
@@ -212,8 +247,7 @@ void register_runtime(py::module_& m) {
       .def("forward",
            [](FusedRing& f, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
               c10::optional<torch::Tensor> lse, double scale) {
-             for (auto* t : {&q, &k, &v, &out})
-               TORCH_CHECK(t->is_cuda() && t->is_contiguous(), "CUDA contiguous tensors required");
+             check_fused_io(f, &q, &k, &v, &out, lse);
              const c10::cuda::CUDAGuard guard(q.device());
              f.forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                        out.scalar_type() == torch::kBFloat16,
@@ -224,12 +258,14 @@ void register_runtime(py::module_& m) {
            py::arg("scale"))
       .def("prepare",
            [](FusedRing& f, torch::Tensor k, torch::Tensor v) {
+             check_fused_io(f, nullptr, &k, &v, nullptr, c10::nullopt);
              const c10::cuda::CUDAGuard guard(k.device());
              f.prepare(k.data_ptr(), v.data_ptr(), at::cuda::getCurrentCUDAStream().stream());
            })
       .def("attend",
            [](FusedRing& f, torch::Tensor q, torch::Tensor out, c10::optional<torch::Tensor> lse,
               double scale) {
+             check_fused_io(f, &q, nullptr, nullptr, &out, lse);
              const c10::cuda::CUDAGuard guard(q.device());
              f.attend(q.data_ptr(), out.data_ptr(), out.scalar_type() == torch::kBFloat16,
                       lse ? lse->data_ptr<float>() : nullptr, static_cast<float>(scale),

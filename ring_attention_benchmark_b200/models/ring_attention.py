@@ -73,13 +73,19 @@ class RingAttention:
     def world(self) -> int:
         return self.runtime.world
 
-    def _check_inputs(self, q, k, v):
+    def _check_inputs(self, q, k, v, out=None):
         exp_q = (self.seq, self.heads, self.head_dim)
         exp_kv = (self.seq, self.heads_kv, self.head_dim)
+        dev = torch.device("cuda", self.runtime.device)
         for name, t, shape in (("q", q, exp_q), ("k", k, exp_kv), ("v", v, exp_kv)):
-            if tuple(t.shape) != shape or t.dtype != self.dtype or not t.is_cuda:
-                raise ValueError(f"{name}: expected CUDA {self.dtype} tensor of shape {shape}, "
+            if tuple(t.shape) != shape or t.dtype != self.dtype or t.device != dev:
+                raise ValueError(f"{name}: expected {self.dtype} tensor of shape {shape} on {dev}, "
                                  f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+        if out is not None and (tuple(out.shape) != exp_q or out.device != dev
+                                or out.dtype not in (torch.float32, torch.bfloat16)
+                                or not out.is_contiguous()):
+            raise ValueError(f"out: expected a contiguous float32/bfloat16 tensor of shape "
+                             f"{exp_q} on {dev}, got {out.dtype} {tuple(out.shape)} on {out.device}")
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  scale: Optional[float] = None, return_lse: bool = False,
@@ -89,7 +95,7 @@ class RingAttention:
         With ``check=True`` the call synchronises and raises if a bounded
         device-side wait ran out (e.g. a peer rank never arrived).
         """
-        self._check_inputs(q, k, v)
+        self._check_inputs(q, k, v, out)
         if scale is None:
             scale = self.head_dim ** -0.5
         if out is None:
@@ -102,6 +108,12 @@ class RingAttention:
         return (out, lse) if return_lse else out
 
     forward = __call__
+
+    def __enter__(self) -> "RingAttention":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
 
     def check(self) -> None:
         self.engine.check()
