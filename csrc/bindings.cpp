@@ -7,6 +7,7 @@
 #include <string>
 
 #include "launchers.h"
+#include "bind_util.h"
 #include "strfmt.h"
 
 namespace rab {
@@ -45,7 +46,7 @@ void umma_selftest(torch::Tensor A, torch::Tensor B, torch::Tensor D, bool a_in_
   RAB_CHECK(D.scalar_type() == torch::kFloat32 && D.size(0) == 128 && D.size(1) == N,
               "D must be fp32 [128, N]");
   const c10::cuda::CUDAGuard guard(A.device());
-  check_launch(umma_selftest_launch(A.data_ptr(), B.data_ptr(), D.data_ptr<float>(), N, K, tf32,
+  check_launch(umma_selftest_launch(A.data_ptr(), B.data_ptr(), f32_ptr(D, "D"), N, K, tf32,
                                     a_in_tmem, b_mn_major, status_ptr(status), cur_stream()),
                "umma_selftest");
 }
@@ -61,12 +62,12 @@ void simt_partial_attention(torch::Tensor Q, torch::Tensor K, torch::Tensor V, t
   const int D = static_cast<int>(Q.size(2));
   const c10::cuda::CUDAGuard guard(Q.device());
   check_launch(simt_partial_attention_launch(
-                   Q.data_ptr<float>(), K.data_ptr<float>(), V.data_ptr<float>(),
+                   f32_ptr(Q, "Q"), f32_ptr(K, "K"), f32_ptr(V, "V"),
                    static_cast<int>(Q.size(0)), static_cast<int>(K.size(0)),
                    static_cast<int>(Q.size(1)), static_cast<int>(K.size(1)), D,
                    static_cast<float>(scale), static_cast<int>(causal_offset),
-                   acc.data_ptr<float>(), m ? m->data_ptr<float>() : nullptr,
-                   l ? l->data_ptr<float>() : nullptr, normalize, cur_stream()),
+                   f32_ptr(acc, "acc"), m ? f32_ptr(*m, "m") : nullptr,
+                   l ? f32_ptr(*l, "l") : nullptr, normalize, cur_stream()),
                "simt_partial_attention");
 }
 
@@ -77,9 +78,9 @@ void merge_lse(torch::Tensor m_run, torch::Tensor l_run, torch::Tensor acc_run, 
   const int rows = static_cast<int>(m_run.numel());
   RAB_CHECK(acc_run.numel() == static_cast<int64_t>(rows) * D, "acc/m shape mismatch");
   const c10::cuda::CUDAGuard guard(m_run.device());
-  check_launch(merge_lse_launch(m_run.data_ptr<float>(), l_run.data_ptr<float>(),
-                                acc_run.data_ptr<float>(), m_new.data_ptr<float>(),
-                                l_new.data_ptr<float>(), acc_new.data_ptr<float>(), rows, D,
+  check_launch(merge_lse_launch(f32_ptr(m_run, "m_run"), f32_ptr(l_run, "l_run"),
+                                f32_ptr(acc_run, "acc_run"), f32_ptr(m_new, "m_new"),
+                                f32_ptr(l_new, "l_new"), f32_ptr(acc_new, "acc_new"), rows, D,
                                 cur_stream()),
                "merge_lse");
 }
@@ -92,8 +93,8 @@ void normalize(torch::Tensor acc, torch::Tensor m, torch::Tensor l, torch::Tenso
   const bool bf16 = out.scalar_type() == torch::kBFloat16;
   RAB_CHECK(bf16 || out.scalar_type() == torch::kFloat32, "out must be fp32 or bf16");
   const c10::cuda::CUDAGuard guard(acc.device());
-  check_launch(normalize_launch(acc.data_ptr<float>(), m.data_ptr<float>(), l.data_ptr<float>(),
-                                out.data_ptr(), bf16, lse ? lse->data_ptr<float>() : nullptr, rows,
+  check_launch(normalize_launch(f32_ptr(acc, "acc"), f32_ptr(m, "m"), f32_ptr(l, "l"),
+                                out.data_ptr(), bf16, lse ? f32_ptr(*lse, "lse") : nullptr, rows,
                                 D, cur_stream()),
                "normalize");
 }
@@ -104,11 +105,11 @@ void cast(torch::Tensor in, torch::Tensor out) {
   RAB_CHECK(in.numel() == out.numel(), "cast: size mismatch");
   const c10::cuda::CUDAGuard guard(in.device());
   if (in.scalar_type() == torch::kFloat32 && out.scalar_type() == torch::kBFloat16) {
-    check_launch(cast_f32_bf16_launch(in.data_ptr<float>(), out.data_ptr(), in.numel(),
+    check_launch(cast_f32_bf16_launch(f32_ptr(in, "in"), out.data_ptr(), in.numel(),
                                       cur_stream()),
                  "cast_f32_bf16");
   } else if (in.scalar_type() == torch::kBFloat16 && out.scalar_type() == torch::kFloat32) {
-    check_launch(cast_bf16_f32_launch(in.data_ptr(), out.data_ptr<float>(), in.numel(),
+    check_launch(cast_bf16_f32_launch(in.data_ptr(), f32_ptr(out, "out"), in.numel(),
                                       cur_stream()),
                  "cast_bf16_f32");
   } else {
@@ -123,8 +124,8 @@ void split_tf32(torch::Tensor in, torch::Tensor big, torch::Tensor small) {
   }
   RAB_CHECK(in.numel() == big.numel() && in.numel() == small.numel(), "split_tf32: size mismatch");
   const c10::cuda::CUDAGuard guard(in.device());
-  check_launch(split_tf32_launch(in.data_ptr<float>(), big.data_ptr<float>(),
-                                 small.data_ptr<float>(), in.numel(), cur_stream()),
+  check_launch(split_tf32_launch(f32_ptr(in, "in"), f32_ptr(big, "big"),
+                                 f32_ptr(small, "small"), in.numel(), cur_stream()),
                "split_tf32");
 }
 

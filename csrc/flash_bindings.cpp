@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 
 #include "flash.h"
+#include "bind_util.h"
 #include "strfmt.h"
 
 namespace rab {
@@ -77,14 +78,14 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
   a.timeout_s = timeout_s;
   if (acc.has_value()) {
     a.partial = true;
-    a.acc = acc->data_ptr<float>();
-    a.m = m ? m->data_ptr<float>() : nullptr;
-    a.l = l ? l->data_ptr<float>() : nullptr;
+    a.acc = f32_ptr(*acc, "acc");
+    a.m = m ? f32_ptr(*m, "m") : nullptr;
+    a.l = l ? f32_ptr(*l, "l") : nullptr;
   } else {
     RAB_CHECK(out.has_value(), "out (or partial acc/m/l) is required");
     a.out = out->data_ptr();
     a.out_bf16 = out->scalar_type() == torch::kBFloat16;
-    a.lse = lse ? lse->data_ptr<float>() : nullptr;
+    a.lse = lse ? f32_ptr(*lse, "lse") : nullptr;
   }
   const FlashPlan pl = flash_plan(a);
   torch::Tensor ws;

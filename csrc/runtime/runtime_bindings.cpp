@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "drivers.h"
+#include "bind_util.h"
 #include "strfmt.h"
 #include "host_comm.h"
 #include "ring_context.h"
@@ -251,7 +252,7 @@ void register_runtime(py::module_& m) {
              const c10::cuda::CUDAGuard guard(q.device());
              f.forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                        out.scalar_type() == torch::kBFloat16,
-                       lse ? lse->data_ptr<float>() : nullptr, static_cast<float>(scale),
+                       lse ? f32_ptr(*lse, "lse") : nullptr, static_cast<float>(scale),
                        at::cuda::getCurrentCUDAStream().stream());
            },
            py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse") = c10::nullopt,
@@ -268,7 +269,7 @@ void register_runtime(py::module_& m) {
              check_fused_io(f, &q, nullptr, nullptr, &out, lse);
              const c10::cuda::CUDAGuard guard(q.device());
              f.attend(q.data_ptr(), out.data_ptr(), out.scalar_type() == torch::kBFloat16,
-                      lse ? lse->data_ptr<float>() : nullptr, static_cast<float>(scale),
+                      lse ? f32_ptr(*lse, "lse") : nullptr, static_cast<float>(scale),
                       at::cuda::getCurrentCUDAStream().stream());
            },
            py::arg("q"), py::arg("out"), py::arg("lse") = c10::nullopt, py::arg("scale"))
