@@ -3,7 +3,8 @@
 #SBATCH --nodes=1
 #SBATCH --gres=gpu:8
 #SBATCH --time=01:00:00
-# batch_slurm.example.sh - one 8xB200 node.  The batch step prepares the run and
+# batch_slurm.example.sh - one 8xB200 node (counterpart of the reference's
+# batch_slurm.example.sh:5-9,54-78).  The batch step prepares the run and
 # starts each sweep with the bundled launcher (one node, NVLink/NVSwitch).
 set -euo pipefail
 cd "${SLURM_SUBMIT_DIR:-$(dirname "$0")}"

@@ -45,7 +45,8 @@ sys.path.insert(0, ROOT)
 METRIC = "ring_attention_fwd_tflops"
 # name: (tokens per rank, q heads, kv heads, head dim, dtype, causal, input scale, seed)
 PRESETS = {
-    # the reference's full ring attention at its largest ATTENTION_SIZES entry (headline)
+    # the reference's full ring attention at its largest ATTENTION_SIZES entry
+    # (config.example.env:31: 1048576 bytes = 16384 fp32 tokens x d=64; headline)
     "ref-fp32": (16384, 1, 1, 64, "fp32", False, 1.0, None),
     # multi-head bf16, causal with zigzag sharding
     "mha-bf16-causal": (16384, 32, 32, 128, "bf16", True, 1.0, None),

@@ -1,5 +1,6 @@
 #!/bin/bash
-# benchmark_attention.sh - ring attention benchmark over backends and sizes.
+# benchmark_attention.sh - ring attention benchmark over backends and sizes
+# (counterpart of the reference's benchmark_attention.sh, backend loop :109-131).
 #
 # Env / benchmark.env keys: NP WARMUP ITERS SIZES ATTENTION_SIZES ATTENTION_BACKENDS LAUNCHER
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN

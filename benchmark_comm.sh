@@ -1,5 +1,6 @@
 #!/bin/bash
-# benchmark_comm.sh - comm-only ring benchmark over backends and sizes.
+# benchmark_comm.sh - comm-only ring benchmark over backends and sizes
+# (counterpart of the reference's benchmark_comm.sh, backend loop :107-129).
 #
 # Env / benchmark.env keys: NP WARMUP ITERS SIZES COMM_SIZES BACKENDS LAUNCHER
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN

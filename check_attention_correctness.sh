@@ -1,6 +1,7 @@
 #!/bin/bash
 # check_attention_correctness.sh - run attention backends with output dumps and
-# compare them.
+# compare them (counterpart of the reference's check_attention_correctness.sh:114-178,
+# PASS rule at :166).
 #
 # Pairs compared with the reference's rule (PASS if max_abs_err <= ABS_TOL or
 # max_rel_err <= REL_TOL): the reference's two pairs (staged_Isendrecv vs its

@@ -1,6 +1,7 @@
 #!/bin/bash
 # collect_env.sh - record the machine, driver, toolchain and library versions a
-# result was measured with.  Read-only: nothing on the GPUs is changed.
+# result was measured with (counterpart of the reference's collect_env.sh:23-147).
+# Read-only: nothing on the GPUs is changed.
 set -uo pipefail
 
 section() { echo ""; echo "===== $* ====="; }

@@ -1,5 +1,7 @@
 // flash_fwd_2q_sm100.cu - bf16 flash-attention forward with two query tiles
-// per CTA (256 query rows), for B200 (sm_100a).
+// per CTA (256 query rows), for B200 (sm_100a).  Like the one-tile kernel it
+// stands in for the reference's row-per-CTA partial attention kernel
+// (src/attention/ring_attention_nccl_gpu_bench.cu:46-111) and its merge (:113-134).
 //
 // With one query tile the chain S_j -> softmax_j -> PV_j is serial: the exp
 // work of a 128x128 tile (MUFU-bound, about as long as its two GEMMs) can hide

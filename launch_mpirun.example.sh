@@ -1,5 +1,6 @@
 #!/bin/bash
 # launch_mpirun.example.sh - the same sweep with an existing MPI installation
+# (counterpart of the reference's launch_mpirun.example.sh:25-48)
 # (mpirun only starts the ranks; they bootstrap through torch.distributed and
 # communicate through the native runtime, not through MPI).
 set -euo pipefail
