@@ -90,6 +90,7 @@ def relaunch(args) -> int:
 
 def main() -> int:
     args = parse()
+    os.environ.setdefault("RAB_CRASH_HANDLER", "1")  # native backtrace on a fatal signal
     if args.impl == "reference":
         return reference_arm(args)
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:

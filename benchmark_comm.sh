@@ -16,11 +16,10 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG NP WARMUP ITERS SIZES COMM_SIZES BACKENDS SIZE_UNIT RESUME RAB_RESULTS_JSONL \
-  LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS
-configure_runtime_env
+rab_load_config "${CONFIG}"
+rab_setup_paths
 
-if under_launcher; then
+if rab_inside_launched_rank; then
   echo "ERROR: benchmark_comm.sh should be run from a normal shell; it launches the ranks itself." >&2
   exit 1
 fi

@@ -18,12 +18,10 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" CONFIG RUN_LABEL RESULTS_ROOT NP SIZE WARMUP ITERS BUILD \
-  LAUNCHER MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS \
-  ABS_TOL REL_TOL ORACLE RAB_DATA RAB_PREC
-configure_runtime_env
+rab_load_config "${CONFIG}"
+rab_setup_paths
 
-if under_launcher; then
+if rab_inside_launched_rank; then
   echo "ERROR: check_attention_correctness.sh should be run from a normal shell." >&2
   exit 1
 fi

@@ -14,6 +14,17 @@ namespace {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// A tensor the kernel writes: contiguous, on `dev`, at least `min_numel`
+// elements.  A short buffer would be written past its end by the kernel (a
+// device fault), so it is refused here as a RuntimeError instead.
+void check_output(const torch::Tensor& t, const char* name, const c10::Device& dev,
+                  int64_t min_numel) {
+  RAB_CHECK(t.is_cuda() && t.device() == dev, "%s must be on the same GPU as q", name);
+  RAB_CHECK(t.is_contiguous(), "%s must be contiguous", name);
+  RAB_CHECK(t.numel() >= min_numel, "%s has %lld elements, needs at least %lld", name,
+            static_cast<long long>(t.numel()), static_cast<long long>(min_numel));
+}
+
 Prec to_prec(int64_t p) {
   RAB_CHECK(p == 0 || p == 1, "prec must be 0 (bf16) or 1 (fp32 via 3xTF32)");
   return static_cast<Prec>(p);
@@ -50,6 +61,10 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
               "q dtype does not match prec");
   RAB_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32 && status.numel() >= 8,
               "status must be int32[8] on the GPU");
+  RAB_CHECK(status.device() == q.device(), "status must be on the same GPU as q");
+  RAB_CHECK(slots.is_cuda() && slots.device() == q.device() && slots.is_contiguous(),
+            "slots must be contiguous on the same GPU as q");
+  const int64_t rows = q.size(0) * q.size(1);  // Sq * Hq
   const c10::cuda::CUDAGuard guard(q.device());
   FlashArgs a;
   a.prec = pr;
@@ -78,13 +93,21 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
   a.timeout_s = timeout_s;
   if (acc.has_value()) {
     a.partial = true;
+    check_output(*acc, "acc", q.device(), rows * q.size(2));
     a.acc = f32_ptr(*acc, "acc");
+    if (m) check_output(*m, "m", q.device(), rows);
+    if (l) check_output(*l, "l", q.device(), rows);
     a.m = m ? f32_ptr(*m, "m") : nullptr;
     a.l = l ? f32_ptr(*l, "l") : nullptr;
   } else {
     RAB_CHECK(out.has_value(), "out (or partial acc/m/l) is required");
+    check_output(*out, "out", q.device(), q.numel());
+    RAB_CHECK(out->sizes() == q.sizes(), "out must have q's shape [Sq, Hq, D]");
+    RAB_CHECK(out->scalar_type() == torch::kBFloat16 || out->scalar_type() == torch::kFloat32,
+              "out must be bfloat16 or float32");
     a.out = out->data_ptr();
     a.out_bf16 = out->scalar_type() == torch::kBFloat16;
+    if (lse) check_output(*lse, "lse", q.device(), rows);
     a.lse = lse ? f32_ptr(*lse, "lse") : nullptr;
   }
   const FlashPlan pl = flash_plan(a);

@@ -30,6 +30,18 @@
 //    the GPU (different streams, no ordering between them) race on it; order
 //    them on one stream or with events.
 //  * the launch is asynchronous on `stream`; 0 means the work was queued.
+//    Every wait inside the kernel is bounded: if one runs out, the kernel
+//    records the error in a status word (also in the scratch array) and
+//    returns, leaving `out` undefined.  Check it with
+//    rab_flash_attention_noalloc_status once the work is due: it waits for
+//    `stream` and returns RAB_NOALLOC_ERR_DEVICE (with the wait site in `err`
+//    and, when `info` is not NULL, code / site / block / detail in info[0..3])
+//    if the last call on this device failed on the GPU.  The status word is
+//    cleared at the start of every call, so read it before the next one.
+//  * rab_flash_attention_noalloc_wait_selftest runs one bounded wait on a
+//    flag that nothing sets against the same status word, so a caller can see
+//    how a device-side timeout surfaces (the status call then reports it);
+//    timeout_s is in (0, 5].
 #pragma once
 
 #include <cuda_runtime.h>
@@ -41,6 +53,7 @@
 #define RAB_NOALLOC_ERR_ARGS (-1)
 #define RAB_NOALLOC_ERR_TOO_LARGE (-2)
 #define RAB_NOALLOC_ERR_CUDA (-3)
+#define RAB_NOALLOC_ERR_DEVICE (-4) /* the kernel reported an error in its status word */
 
 #ifdef __cplusplus
 extern "C" {
@@ -50,6 +63,12 @@ int rab_flash_attention_noalloc(const void* q, const void* k, const void* v, voi
                                 float* lse, int Sq, int Skv, int Hq, int Hkv, int D, float scale,
                                 int causal, int nsplit, cudaStream_t stream, char* err,
                                 size_t err_len);
+
+int rab_flash_attention_noalloc_status(cudaStream_t stream, unsigned int* info, char* err,
+                                       size_t err_len);
+
+int rab_flash_attention_noalloc_wait_selftest(double timeout_s, cudaStream_t stream, char* err,
+                                              size_t err_len);
 
 #ifdef __cplusplus
 }

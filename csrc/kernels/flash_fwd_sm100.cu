@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 #include <cstring>
@@ -873,19 +874,20 @@ int launch_impl(const FlashParams& p, const FlashMaps& maps, int grid, bool coop
 }  // namespace
 
 int flash_sm_count() {
-  // per device (a process may drive GPUs of different sizes, or MIG slices)
-  static int cache[64] = {};
+  // per device (a process may drive GPUs of different sizes, or MIG slices);
+  // atomic because host threads of the C entry points may call this at once
+  static std::atomic<int> cache[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (cache[dev] == 0) {
-    int sms = 0;
+  int sms = cache[dev].load(std::memory_order_relaxed);
+  if (sms == 0) {
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         sms <= 0)
       sms = 148;  // B200 (query failed)
-    cache[dev] = sms;
+    cache[dev].store(sms, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return sms;
 }
 
 size_t ring_v_offset(Prec prec, int Skv, int Hkv, int D) {

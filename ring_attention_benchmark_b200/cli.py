@@ -165,6 +165,8 @@ def attention_main(backend: str, argv: List[str]) -> int:
 
 def program_main(prog: str, argv: List[str]) -> int:
     """Dispatch on the program name used by the reference (bin/<name>)."""
+    # a program (not a library import) asks for the native backtrace on a fatal signal
+    os.environ.setdefault("RAB_CRASH_HANDLER", "1")
     name = os.path.basename(prog)
     if name.startswith("ring_loop_"):
         return comm_main(name[len("ring_loop_"):], argv)

@@ -1,11 +1,12 @@
 """``benchmark.env`` handling for Python tools.
 
-The shell scripts source the file with ``source_config_preserving_env`` (in
-``ring_env.sh``): variables already set in the environment win over the file,
-the precedence of the reference's ``scripts/mpi_env.sh`` (lines 126-153).  This
-module applies the same rule to the same ``KEY=value`` syntax (optional quotes,
-``#`` comments, ``export`` prefix) so Python tools and tests see the values the
-scripts would.
+Precedence: a variable already set in the environment wins over the file,
+the rule of the reference's ``scripts/mpi_env.sh`` (lines 126-153).  This
+module is the one parser of the ``KEY=value`` syntax (optional quotes, ``#``
+comments, ``export`` prefix; the file is parsed, never executed): Python tools
+call `load_config`, and the shell scripts' ``rab_load_config`` (in
+``ring_env.sh``) reads the file through ``config.py --dump`` and applies the
+same rule, so both see the same values.
 
 Size lists: the reference's wrappers read ``SIZES`` only, so ``COMM_SIZES`` /
 ``ATTENTION_SIZES`` from the config never reached them
@@ -78,3 +79,27 @@ def sizes_for(run_type: str, cfg: Mapping[str, str]) -> List[int]:
         return [int(s) for s in cfg["SIZES"].split()]
     key = "COMM_SIZES" if run_type == "comm" else "ATTENTION_SIZES"
     return [int(s) for s in cfg.get(key, DEFAULTS[key]).split()]
+
+
+def _main(argv: List[str]) -> int:
+    """``python config.py --dump FILE``: one ``KEY<TAB>value`` line per key of
+    FILE, for ``rab_load_config`` in ``ring_env.sh`` (run as a plain script, so
+    no package or torch import happens)."""
+    import sys
+
+    if len(argv) != 2 or argv[0] != "--dump":
+        print("usage: config.py --dump FILE", file=sys.stderr)
+        return 2
+    for key, val in parse_env_file(argv[1]).items():
+        if "\t" in val or "\n" in val:
+            print(f"config.py: {key}: tabs and newlines are not supported in values",
+                  file=sys.stderr)
+            return 1
+        print(f"{key}\t{val}")
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+
+    sys.exit(_main(sys.argv[1:]))

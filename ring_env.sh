@@ -1,101 +1,73 @@
 #!/bin/bash
 # ring_env.sh - shell helpers shared by the benchmark scripts (sourced, not run).
 #
-#   configure_runtime_env            PATH / LD_LIBRARY_PATH from CUDA_HOME, NCCL_HOME, MPI_HOME
-#   detect_world_rank / _size        rank variables set by mpirun, srun, PMI, torchrun
-#   under_launcher                   true inside a launched rank (the scripts refuse to run there)
-#   source_config_preserving_env F K...  source config F; variables K already set keep their value
+#   rab_load_config FILE             apply FILE's KEY=value settings; variables already
+#                                    set in the shell or environment keep their value
+#   rab_setup_paths                  PATH / LD_LIBRARY_PATH from CUDA_HOME, NCCL_HOME, MPI_HOME
+#   rab_inside_launched_rank         true inside a rank started by mpirun, srun, PMI or
+#                                    torchrun (the scripts refuse to run there: they
+#                                    start the ranks themselves)
+#   size_to_bytes SIZE               configured size -> the programs' byte argument
 #   launch_ranks NP CMD...           start NP ranks of CMD with the selected LAUNCHER
 #
-# Same precedence rule as the reference's scripts/mpi_env.sh: the environment
-# overrides the config file.
+# Precedence is the reference's (scripts/mpi_env.sh): the environment overrides
+# the config file.  The file is parsed by utils/config.py, the parser the
+# Python tools use, so scripts and tools agree on every value.
 
 RAB_ROOT="${RAB_ROOT:-$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)}"
 RAB_PYTHON="${RAB_PYTHON:-$(command -v python3 || command -v python)}"
 
-path_contains() {
-  local needle="$1" value="$2" entry=""
-  local -a entries=()
-  [ -z "${value}" ] && return 1
-  IFS=':' read -r -a entries <<< "${value}"
-  for entry in "${entries[@]}"; do
-    [ "${entry}" = "${needle}" ] && return 0
+rab_load_config() {
+  local file="$1" key value listing
+  [ -f "${file}" ] || return 0
+  listing="$("${RAB_PYTHON}" "${RAB_ROOT}/ring_attention_benchmark_b200/utils/config.py" \
+    --dump "${file}")" || return 1
+  while IFS=$'\t' read -r key value; do
+    [ -n "${key}" ] || continue
+    # set already (even to an empty string): the shell's value wins
+    [ -n "${!key+set}" ] && continue
+    declare -gx "${key}=${value}"
+  done <<< "${listing}"
+}
+
+# _rab_path_add VAR DIR: put DIR in front of the colon list VAR unless it is
+# already listed or does not exist.
+_rab_path_add() {
+  local var="$1" dir="$2" list
+  [ -n "${dir}" ] && [ -d "${dir}" ] || return 0
+  list="${!var:-}"
+  case ":${list}:" in
+    *":${dir}:"*) return 0 ;;
+  esac
+  declare -gx "${var}=${dir}${list:+:${list}}"
+}
+
+rab_setup_paths() {
+  local home
+  for home in "${CUDA_HOME:-}" "${MPI_HOME:-}"; do
+    [ -n "${home}" ] && _rab_path_add PATH "${home}/bin"
+  done
+  [ -n "${CUDA_HOME:-}" ] && _rab_path_add LD_LIBRARY_PATH "${CUDA_HOME}/lib64"
+  for home in "${NCCL_HOME:-}" "${MPI_HOME:-}"; do
+    [ -n "${home}" ] && _rab_path_add LD_LIBRARY_PATH "${home}/lib"
+  done
+  if [ -z "${MPIRUN:-}" ] && [ -n "${MPI_HOME:-}" ] && [ -x "${MPI_HOME}/bin/mpirun" ]; then
+    declare -gx MPIRUN="${MPI_HOME}/bin/mpirun"
+  fi
+  return 0
+}
+
+# Rank variables exported by the launchers this suite knows (Open MPI, PMIx,
+# MPICH/Hydra PMI, MVAPICH2, Slurm); torchrun is recognised by its run id.
+_RAB_RANK_VARS=(OMPI_COMM_WORLD_RANK OMPI_COMM_WORLD_SIZE PMIX_RANK PMI_RANK PMI_SIZE
+                MV2_COMM_WORLD_RANK SLURM_PROCID TORCHELASTIC_RUN_ID)
+
+rab_inside_launched_rank() {
+  local name
+  for name in "${_RAB_RANK_VARS[@]}"; do
+    [ -n "${!name:-}" ] && return 0
   done
   return 1
-}
-
-prepend_path_var() {
-  local var_name="$1" dir="$2"
-  local current="${!var_name:-}"
-  if [ -z "${dir}" ] || [ ! -d "${dir}" ]; then return 0; fi
-  if path_contains "${dir}" "${current}"; then return 0; fi
-  if [ -n "${current}" ]; then
-    printf -v "${var_name}" '%s:%s' "${dir}" "${current}"
-  else
-    printf -v "${var_name}" '%s' "${dir}"
-  fi
-  export "${var_name?}"
-}
-
-configure_runtime_env() {
-  if [ -n "${CUDA_HOME:-}" ]; then
-    prepend_path_var PATH "${CUDA_HOME}/bin"
-    prepend_path_var LD_LIBRARY_PATH "${CUDA_HOME}/lib64"
-  fi
-  if [ -n "${NCCL_HOME:-}" ]; then
-    prepend_path_var LD_LIBRARY_PATH "${NCCL_HOME}/lib"
-  fi
-  if [ -n "${MPI_HOME:-}" ]; then
-    prepend_path_var PATH "${MPI_HOME}/bin"
-    prepend_path_var LD_LIBRARY_PATH "${MPI_HOME}/lib"
-    if [ -z "${MPIRUN:-}" ] && [ -x "${MPI_HOME}/bin/mpirun" ]; then
-      MPIRUN="${MPI_HOME}/bin/mpirun"
-      export MPIRUN
-    fi
-  fi
-}
-
-detect_world_rank() {
-  local v
-  for v in "${OMPI_COMM_WORLD_RANK:-}" "${PMIX_RANK:-}" "${PMI_RANK:-}" \
-           "${MV2_COMM_WORLD_RANK:-}" "${SLURM_PROCID:-}" "${TORCHELASTIC_RUN_ID:+${RANK:-}}"; do
-    if [ -n "${v}" ]; then printf '%s\n' "${v}"; return 0; fi
-  done
-  return 1
-}
-
-detect_world_size() {
-  local v
-  for v in "${OMPI_COMM_WORLD_SIZE:-}" "${PMIX_SIZE:-}" "${PMI_SIZE:-}" \
-           "${MV2_COMM_WORLD_SIZE:-}" "${SLURM_NTASKS:-}"; do
-    if [ -n "${v}" ]; then printf '%s\n' "${v}"; return 0; fi
-  done
-  return 1
-}
-
-under_launcher() {
-  detect_world_rank >/dev/null 2>&1 || detect_world_size >/dev/null 2>&1
-}
-
-source_config_preserving_env() {
-  local config_path="$1"
-  shift
-  [ -f "${config_path}" ] || return 0
-  local -a restore=()
-  local name quoted
-  for name in "$@"; do
-    if [ "${!name+x}" = "x" ]; then
-      printf -v quoted '%q' "${!name}"
-      restore+=("${name}=${quoted}" "export ${name}")
-    fi
-  done
-  set -a
-  # shellcheck disable=SC1090
-  source "${config_path}"
-  set +a
-  for name in "${restore[@]}"; do
-    eval "${name}"
-  done
 }
 
 # size_to_bytes SIZE: the programs take a shard size in bytes, as the

@@ -10,11 +10,8 @@ cd "${SCRIPT_DIR}"
 source "${SCRIPT_DIR}/ring_env.sh"
 
 CONFIG=${CONFIG:-benchmark.env}
-source_config_preserving_env "${CONFIG}" \
-  CONFIG RUN_LABEL RESULTS_ROOT NP_LIST RUN_TYPES WARMUP ITERS BACKENDS ATTENTION_BACKENDS \
-  COMM_SIZES ATTENTION_SIZES BUILD COLLECT_ENV LAUNCHER HOSTFILE MPIRUN MPIRUN_EXTRA_ARGS \
-  SRUN SRUN_MPI_TYPE SRUN_EXTRA_ARGS RAB_DATA RAB_PREC SIZE_UNIT
-configure_runtime_env
+rab_load_config "${CONFIG}"
+rab_setup_paths
 
 RUN_LABEL=${RUN_LABEL:-"$(hostname)_$(date +%Y%m%d_%H%M%S)"}
 RESULTS_ROOT=${RESULTS_ROOT:-"${SCRIPT_DIR}/results"}
@@ -99,7 +96,7 @@ write_launch_examples() {
   } > "${RUN_DIR}/launch_examples.txt"
 }
 
-if under_launcher; then
+if rab_inside_launched_rank; then
   echo "ERROR: run_suite.sh is preparation-only; run it from a normal shell." >&2
   exit 1
 fi

@@ -89,12 +89,38 @@ def test_scripts_parse(script):
 
 
 def test_env_overrides_config_in_shell(tmp_path):
+    """rab_load_config: a variable set in the shell (exported or not) or in the
+    environment keeps its value; the file fills in the rest, exported; quoted
+    values, comments and `export` prefixes parse as in the Python tools."""
     f = tmp_path / "c.env"
-    f.write_text('NP=4\nWARMUP=9\n')
-    cmd = (f"source {ROOT}/ring_env.sh; NP=2; "
-           f"source_config_preserving_env {f} NP WARMUP; echo $NP $WARMUP")
+    f.write_text('NP=4\nWARMUP=9\n# ITERS=1\nexport BACKENDS="nccl b200_fused"  # two\n'
+                 'ITERS=50\nSIZES=\n')
+    cmd = (f"source {ROOT}/ring_env.sh; NP=2; SIZES=7; "
+           f"rab_load_config {f}; echo $NP $WARMUP $ITERS $SIZES; echo $BACKENDS; "
+           "bash -c 'echo $WARMUP'")
+    env = dict(os.environ, ITERS="3")
+    env.pop("WARMUP", None)
+    r = subprocess.run(["bash", "-c", cmd], capture_output=True, text=True, env=env)
+    lines = r.stdout.splitlines()
+    assert lines[0].split() == ["2", "9", "3", "7"], r.stderr
+    assert lines[1] == "nccl b200_fused"
+    assert lines[2] == "9"  # exported to child processes
+    from ring_attention_benchmark_b200.utils.config import load_config
+    cfg = load_config(str(f), env={"NP": "2", "ITERS": "3"})
+    assert (cfg["NP"], cfg["WARMUP"], cfg["ITERS"], cfg["BACKENDS"]) == ("2", "9", "3",
+                                                                         "nccl b200_fused")
+
+
+def test_path_setup_prepends_once(tmp_path):
+    home = tmp_path / "cuda"
+    (home / "bin").mkdir(parents=True)
+    (home / "lib64").mkdir()
+    cmd = (f"source {ROOT}/ring_env.sh; export CUDA_HOME={home}; PATH=/usr/bin:/bin; "
+           "LD_LIBRARY_PATH=; rab_setup_paths; rab_setup_paths; echo $PATH; echo $LD_LIBRARY_PATH")
     r = subprocess.run(["bash", "-c", cmd], capture_output=True, text=True)
-    assert r.stdout.split() == ["2", "9"]
+    path, ld = r.stdout.splitlines()
+    assert path == f"{home}/bin:/usr/bin:/bin"
+    assert ld == f"{home}/lib64"
 
 
 def test_size_unit_conversion():
