@@ -121,11 +121,15 @@ def main() -> int:
     # before any pinned host buffer exists: keep host<->device copies on the GPU's socket
     from ring_attention_benchmark_b200.utils.affinity import bind_to_gpu
     host_affinity = bind_to_gpu(rt.device)
-    x = inputs.normal_inputs(rank, seq, heads, head_dim, heads_kv=heads_kv,
-                             seed=None if seed is None else seed + rank, mult=mult)
-    q = x.q.to(dev, dtype).contiguous()
-    k = x.k.to(dev, dtype).contiguous()
-    v = x.v.to(dev, dtype).contiguous()
+    def gen(r):  # rank r's inputs, drawn on this GPU (any rank can redraw any other's)
+        return inputs.normal_inputs_device(r, seq, heads, head_dim, heads_kv=heads_kv,
+                                           seed=r if seed is None else seed + r, mult=mult,
+                                           dtype=dtype, device=dev)
+
+    x = gen(rank)
+    q = x.q.contiguous()
+    k = x.k.contiguous()
+    v = x.v.contiguous()
     out = torch.empty_like(q)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -177,9 +181,9 @@ def main() -> int:
     # serving loop runs; the K-step loop is timed as a whole and divided by K.
     e2e = None
     if not args.no_e2e:
-        q_h = x.q.to(dtype).pin_memory()
-        k_h = x.k.to(dtype).pin_memory()
-        v_h = x.v.to(dtype).pin_memory()
+        q_h = q.cpu().pin_memory()
+        k_h = k.cpu().pin_memory()
+        v_h = v.cpu().pin_memory()
         outs_h = [torch.empty(q.shape, dtype=dtype).pin_memory() for _ in range(2)]
         ins = [(torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)) for _ in range(2)]
         outs_d = [torch.empty_like(q) for _ in range(2)]
@@ -240,6 +244,25 @@ def main() -> int:
                "schedule": "H2D of step i+1 and D2H of step i-1 overlap step i on two copy "
                            "streams; K-step loop timed as a whole"}
 
+    # ---- output check: sampled rows of every rank vs a float64 recomputation ----
+    # over the K/V of ALL ranks, regenerated from their seeds on this GPU (not
+    # read through the ring), outside every timed region
+    from ring_attention_benchmark_b200.utils.verify import ring_output_error
+
+    def kv_of(r):
+        if r == rank:
+            return k, v
+        y = gen(r)
+        return y.k, y.v
+
+    err_local = ring_output_error(out, q, rank, world, kv_of, x.scale, causal=causal,
+                                  zigzag=causal, n_rows=256)
+    max_err = rt.reduce_max([err_local])[0]
+    tol = 2e-5 if dt == "fp32" else 2e-2
+    check = {"max_abs_err": max_err, "tol": tol, "passed": bool(max_err <= tol),
+             "rows_per_rank": 256, "heads": "all",
+             "oracle": "float64 over all ranks' K/V regenerated from their seeds (max over ranks)"}
+
     nsplit = attn.engine.nsplit
     # ring-format prep (fp32, one launch), the fused kernel, the merge pass (split or balanced)
     per_step = (1 if dt == "fp32" else 0) + 1 + (1 if nsplit != 1 else 0)
@@ -267,8 +290,10 @@ def main() -> int:
                 "kv_block_elements_per_rank": seq * heads_kv * head_dim,
                 "parallelism": f"cp{world} (ring over NVLink, fused in-kernel transfer, "
                                f"{args.ring_mode} mode)",
-                "data_init": (f"iid N(0,1) x {mult}, seed={'rank' if seed is None else f'{seed}+rank'}, "
+                "data_init": (f"iid N(0,1) x {mult} from the CUDA generator seeded "
+                              f"{'rank' if seed is None else f'{seed}+rank'}, "
                               f"scale 1/sqrt({head_dim})"),
+                "check": check,
                 "l2": "256 MiB buffer written between timed steps (outside the events)",
                 "host_affinity": host_affinity,
                 "flops_per_step_total": flops_total,
@@ -281,8 +306,11 @@ def main() -> int:
             "gpu_launches": per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
+        if not check["passed"]:
+            print(f"bench.py: output check failed: max abs err {max_err:.3g} > {tol:g}",
+                  file=sys.stderr)
     attn.close()
-    return 0
+    return 0 if check["passed"] else 1
 
 
 if __name__ == "__main__":

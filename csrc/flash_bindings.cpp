@@ -125,6 +125,101 @@ std::vector<int64_t> flash_fwd(int64_t prec, torch::Tensor q, torch::Tensor slot
   return {pl.balanced ? -1 : pl.nsplit, pl.n_items, pl.grid};
 }
 
+// The fused ring kernel run as rank `rank` of an emulated `world`-rank ring on
+// ONE GPU: `blocks` holds every rank's ring-format slot-0 block
+// ([world][slot_bytes] uint8); the "peer" slots and flag words the copy warps
+// read are regions of this GPU's memory, with each peer's slot0_ready word
+// set to the launch's epoch before the kernel starts and no peer reads to wait
+// for.  Everything else - the copy role's slices, the per-block arrival
+// counters, the TMA thread's waits on them, the generic->async proxy fence
+// before TMA reads the copied bytes, the cooperative launch - is the code
+// path of a real multi-GPU launch.  Direct mode (block s from its origin's
+// slot 0).
+std::vector<int64_t> flash_fused_loopback(int64_t prec, torch::Tensor q, torch::Tensor blocks,
+                                          int64_t world, int64_t rank, int64_t Skv, int64_t Hkv,
+                                          torch::Tensor out, c10::optional<torch::Tensor> lse,
+                                          double scale, bool causal, bool zigzag,
+                                          torch::Tensor status, double timeout_s) {
+  const Prec pr = to_prec(prec);
+  RAB_CHECK(q.is_cuda() && q.is_contiguous() && q.dim() == 3, "q must be contiguous [Sq, Hq, D]");
+  RAB_CHECK(q.scalar_type() == (pr == Prec::kBF16 ? torch::kBFloat16 : torch::kFloat32),
+            "q dtype does not match prec");
+  RAB_CHECK(world >= 2 && world <= kMaxRanks && rank >= 0 && rank < world,
+            "need 2 <= world <= %d and 0 <= rank < world", kMaxRanks);
+  RAB_CHECK(status.is_cuda() && status.device() == q.device() &&
+                status.scalar_type() == torch::kInt32 && status.numel() >= 8,
+            "status must be int32[8] on q's GPU");
+  const int64_t rows = q.size(0) * q.size(1);
+  check_output(out, "out", q.device(), q.numel());
+  RAB_CHECK(out.sizes() == q.sizes() &&
+                (out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32),
+            "out must be bfloat16/float32 with q's shape");
+  if (lse) check_output(*lse, "lse", q.device(), rows);
+  const size_t bb = ring_block_bytes(pr, static_cast<int>(Skv), static_cast<int>(Hkv),
+                                     static_cast<int>(q.size(2)));
+  RAB_CHECK(blocks.is_cuda() && blocks.device() == q.device() && blocks.is_contiguous() &&
+                static_cast<size_t>(blocks.numel() * blocks.element_size()) >= bb * world,
+            "blocks must hold world ring-format blocks on q's GPU");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const auto u8 = torch::dtype(torch::kUInt8).device(q.device());
+  // this rank's ring slots; slot 0 = its own block
+  torch::Tensor local = torch::empty({static_cast<int64_t>(bb * world)}, u8);
+  uint8_t* src = static_cast<uint8_t*>(blocks.data_ptr());
+  local.narrow(0, 0, bb).copy_(blocks.narrow(0, rank * bb, bb));
+  // flag words: row 0 this rank's, row 1 + r emulated peer r's (slot0_ready = epoch 1)
+  torch::Tensor flags = torch::zeros({world + 1, 128}, torch::dtype(torch::kInt64).device(q.device()));
+  flags.narrow(0, 1, world).select(1, kFlagSlot0Ready).fill_(1);
+  uint64_t* fl = reinterpret_cast<uint64_t*>(flags.data_ptr());
+
+  FlashArgs a;
+  a.prec = pr;
+  a.q = q.data_ptr();
+  a.Sq = q.size(0);
+  a.Hq = q.size(1);
+  a.D = q.size(2);
+  a.Hkv = static_cast<int>(Hkv);
+  a.Skv = static_cast<int>(Skv);
+  a.nblk = static_cast<int>(world);
+  a.scale = static_cast<float>(scale);
+  uint8_t* base = static_cast<uint8_t*>(local.data_ptr());
+  a.k_base = base;
+  a.v_base = base + ring_v_offset(pr, a.Skv, a.Hkv, a.D);
+  a.slot_stride = bb;
+  a.causal = causal;
+  a.zigzag = zigzag;
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.out = out.data_ptr();
+  a.out_bf16 = out.scalar_type() == torch::kBFloat16;
+  a.lse = lse ? f32_ptr(*lse, "lse") : nullptr;
+  a.status = reinterpret_cast<DeviceStatus*>(status.data_ptr());
+  a.timeout_s = timeout_s;
+  a.fused = true;
+  a.local_slots = base;
+  a.slot_bytes = bb;
+  a.flags_local = fl;
+  for (int r = 0; r < world; ++r) {
+    a.peer_slots[r] = r == rank ? base : src + static_cast<size_t>(r) * bb;
+    a.flags_peer[r] = r == rank ? fl : fl + static_cast<size_t>(1 + r) * 128;
+  }
+  const FlashPlan pl = flash_plan(a);
+  a.epoch = 1;
+  a.arrive_target = static_cast<uint64_t>(pl.grid);  // one slice per CTA and block
+  a.reads_target = 0;                                 // no peer reads this rank's slots
+  torch::Tensor ws;
+  if (pl.workspace_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(pl.workspace_bytes)}, u8);
+    a.workspace = ws.data_ptr();
+    a.workspace_bytes = pl.workspace_bytes;
+  }
+  const int err = flash_run(a, pl, cur_stream());
+  RAB_CHECK(err == 0, "fused loopback launch failed: %s",
+            cudaGetErrorString(static_cast<cudaError_t>(err)));
+  // keep the buffers alive until the kernel is done with them
+  c10::cuda::getCurrentCUDAStream().synchronize();
+  return {pl.balanced ? -1 : pl.nsplit, pl.n_items, pl.grid, pl.rows_per_unit};
+}
+
 }  // namespace
 }  // namespace rab
 
@@ -210,4 +305,10 @@ void register_flash(pybind11::module_& m) {
         py::arg("acc") = c10::nullopt, py::arg("m") = c10::nullopt, py::arg("l") = c10::nullopt,
         py::arg("status"), py::arg("timeout_s") = 10.0, py::arg("grid") = 0);
   m.def("sm_count", &rab::flash_sm_count);
+  m.def("flash_fused_loopback", &rab::flash_fused_loopback,
+        "fused ring kernel as one rank of an emulated ring on one GPU (peers in local memory)",
+        py::arg("prec"), py::arg("q"), py::arg("blocks"), py::arg("world"), py::arg("rank"),
+        py::arg("Skv"), py::arg("Hkv"), py::arg("out"), py::arg("lse") = c10::nullopt,
+        py::arg("scale") = 1.0, py::arg("causal") = false, py::arg("zigzag") = false,
+        py::arg("status"), py::arg("timeout_s") = 10.0);
 }

@@ -76,3 +76,29 @@ def size_to_seq(kv_size_bytes: int, dim: int = 64, elem_bytes: int = 4) -> int:
     if kv_size_bytes <= 0 or kv_size_bytes % (dim * elem_bytes):
         raise ValueError(f"kv_size_bytes must be a positive multiple of {dim * elem_bytes}")
     return kv_size_bytes // (dim * elem_bytes)
+
+
+def normal_inputs_device(
+    rank: int,
+    seq: int,
+    heads: int = 1,
+    dim: int = 64,
+    heads_kv: Optional[int] = None,
+    seed: Optional[int] = None,
+    mult: float = 1.0,
+    dtype: torch.dtype = torch.float32,
+    device="cuda",
+) -> AttnInputs:
+    """`normal_inputs` drawn on the GPU from a seeded ``torch.Generator`` of
+    that device (Philox; the same values on every GPU for the same seed), so
+    any rank can regenerate any other rank's inputs in milliseconds - the
+    benchmark's output check rebuilds the whole ring's K/V this way.  Values
+    differ from the CPU generator's for the same seed."""
+    hk = heads if heads_kv is None else heads_kv
+    g = torch.Generator(device=device).manual_seed(rank if seed is None else seed)
+    q = torch.randn(seq, heads, dim, generator=g, device=device) * mult
+    k = torch.randn(seq, hk, dim, generator=g, device=device) * mult
+    v = torch.randn(seq, hk, dim, generator=g, device=device) * mult
+    return AttnInputs(
+        q=q.to(dtype), k=k.to(dtype), v=v.to(dtype), scale=dim ** -0.5, kv_shared=False
+    )
