@@ -183,6 +183,14 @@ State& S() {
   return s;
 }
 
+// Remove this job's shared-memory names this rank knows of (an ending job
+// leaves nothing behind in /dev/shm; existing mappings stay valid).
+void unlink_names() {
+  State& s = S();
+  for (const auto& n : s.chan_names) shm_unlink(n.c_str());
+  if (!s.job.empty()) shm_unlink(("/mmpi_" + s.job).c_str());
+}
+
 [[noreturn]] void die(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -197,6 +205,7 @@ State& S() {
     if (S().hdr->abort_code.compare_exchange_strong(expected, code + 1))
       S().hdr->abort_rank.store(S().rank);
   }
+  unlink_names();
   _exit(code);
 }
 
@@ -214,6 +223,8 @@ void check_abort() {
     fprintf(stderr, "[minimpi] rank %d: rank %d called MPI_Abort(%d); exiting\n", S().rank,
             h->abort_rank.load(), c - 1);
     fflush(stderr);
+    fflush(stdout);
+    unlink_names();
     _exit(c - 1);
   }
 }
@@ -680,6 +691,7 @@ int MPI_Abort(MPI_Comm, int errorcode) {
     if (s.hdr->abort_code.compare_exchange_strong(expected, errorcode + 1))
       s.hdr->abort_rank.store(s.rank);
   }
+  unlink_names();
   _exit(errorcode);
 }
 

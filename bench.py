@@ -56,12 +56,6 @@ PRESETS = {
     "gqa-bf16-long": (65536, 32, 8, 128, "bf16", True, 0.5, 1234),
 }
 L2_FLUSH_BYTES = 256 << 20
-REFERENCE_UNAVAILABLE = (
-    "the reference is a set of MPI programs (every source includes <mpi.h>) with no Python "
-    "package; pip cannot install it (no setup.py/pyproject.toml) and this image has no MPI "
-    "(no mpicxx, mpi.h or libmpi), so its binaries cannot be built or run")
-
-
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -75,10 +69,108 @@ def parse():
     return ap.parse_args()
 
 
+# The reference's attention programs compared with this framework's fused
+# ring: its NCCL program and its best overlapped MPI program (CUDA-aware
+# Isend/Irecv, the data moved GPU to GPU).
+REFERENCE_BACKENDS = ("nccl", "cuda_aware_Isendrecv_overlap")
+
+
 def reference_arm(args) -> int:
+    """The unmodified reference programs (built by baseline/reference_arm.py with
+    their own Makefile) on the same workload: 16384 fp32 tokens x d=64 per rank
+    (kv_size = 4194304 bytes on their command line), one process per GPU.
+    Its metric is turned into this one: 4*S*(N*S)*64 FLOPs per rank over its
+    avg_total (host wall clock per iteration, max over ranks)."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import reference_arm as ra
+
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    def unavailable(why):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return 0
+
+    seq, heads, heads_kv, head_dim, dt, causal, _, _ = PRESETS[args.preset]
+    seq = args.seq or seq
+    if (heads, heads_kv, head_dim, dt, causal) != (1, 1, 64, "fp32", False):
+        return unavailable("the reference computes single-head fp32 d=64 non-causal attention "
+                           f"only; preset {args.preset} has no counterpart")
+    missing = [b for b in REFERENCE_BACKENDS
+               if not os.path.exists(ra.program(f"ring_attention_{b}_gpu_bench"))]
+    if missing and rank == 0 and os.path.isdir(ra.REF_SRC_DIR):
+        try:  # same image on every machine: rebuild from the copied sources
+            ra.install()
+        except Exception as exc:  # reported below through `missing`
+            print(f"bench.py: reference build failed: {exc}", file=sys.stderr)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=3600))
+        dist.barrier()
+    missing = [b for b in REFERENCE_BACKENDS
+               if not os.path.exists(ra.program(f"ring_attention_{b}_gpu_bench"))]
+    if missing:
+        return unavailable(f"reference programs not built ({', '.join(missing)}); run "
+                           "`python baseline/reference_arm.py install`")
+    from ring_attention_benchmark_b200.utils.clocks import ClockSampler
+
+    kv_bytes = seq * head_dim * 4
+    sampler = ClockSampler(gpus=list(range(world)))
     if rank == 0:
-        print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+        sampler.start()
+    per_backend, first_fail = {}, None
+    for b in REFERENCE_BACKENDS:
+        work = os.path.join(ROOT, "baseline", "_ref", "run", f"{b}_np{world}_rank{rank}")
+        rc, out, err = ra.run_attention(b, kv_bytes, args.warmup, args.steps, work)
+        ms = ra.parse_avg_total_ms(out) if rank == 0 else None
+        if rank == 0:
+            if rc != 0 or ms is None:
+                tail = (out.strip().splitlines() or err.strip().splitlines() or ["no output"])
+                first_fail = first_fail or f"{b}: exit {rc}: {tail[-1].strip()}"
+            else:
+                per_backend[b] = {"avg_total_ms": ms, "summary": out.strip().splitlines()[-2:]}
+    clocks = sampler.stop() if rank == 0 else None
+    if rank != 0:
+        return 0
+    if not per_backend:
+        return unavailable(f"the reference's own programs did not produce a result: {first_fail}")
+    flops_total = 4.0 * seq * (world * seq) * head_dim * world
+    for b, r in per_backend.items():
+        r["tflops"] = round(flops_total / (r["avg_total_ms"] * 1e-3) / 1e12, 4)
+    best = min(per_backend, key=lambda b: per_backend[b]["avg_total_ms"])
+    ms = per_backend[best]["avg_total_ms"]
+    value = round(flops_total / (ms * 1e-3) / 1e12, 4)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (the reference's own inputs: K = V = rank*1000 + i, its Q formula)",
+        "config": {
+            "model": "ring attention fwd, 1 head, d=64, non-causal, fp32 (the reference's "
+                     "row-per-CTA CUDA-core kernel and merge kernel)",
+            "global_batch": 1, "seq_len": world * seq, "seq_per_rank": seq,
+            "kv_size_bytes_arg": kv_bytes, "parallelism": f"cp{world} (reference ring)",
+            "backend": best, "per_backend": per_backend,
+            "build": f"reference Makefile `make all`, NVCCFLAGS='{ra.NVCCFLAGS}', MPI_HOME="
+                     "baseline/minimpi build (MPI subset: shared memory, CUDA IPC), NCCL from "
+                     "torch",
+            "timing": "the reference's avg_total: host wall clock per iteration, max over "
+                      "ranks (its MPI_Reduce MAX), averaged over its timed iterations; it "
+                      "includes its device-to-host copy of acc/l and host normalisation",
+            "flops_per_step_total": flops_total,
+        },
+        "clocks": clocks,
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": seq * head_dim * 4 + seq * 4,
+                "note": "the reference's own avg_total already ends with its D2H of acc and l "
+                        "and the host normalisation; its inputs are created on the host once"},
+        "gpu_launches": 2 * world * args.steps,
+    }
+    print(json.dumps(line), flush=True)
     return 0
 
 

@@ -112,6 +112,16 @@ CUtensorMap flash_make_q_map(const void* q, int Sq, int Hq, int D);
 int flash_forward_2q_launch(const FlashParams& p, const CUtensorMap& tmq, const FlashMaps& maps,
                             int grid, bool cooperative, cudaStream_t stream);
 
+// bf16 d=128 kernel on CTA pairs (clusters of two, tcgen05 cta_group::2):
+// 512-row work units; each CTA loads half of every K/V tile.  k_base/v_base
+// and slot_stride describe the ring slots as for flash_make_maps.  `grid` must
+// be even and at most flash_pair_max_grid() when every CTA has to be resident
+// (fused mode).
+int flash_forward_2sm_launch(const FlashParams& p, const CUtensorMap& tq, const void* k_base,
+                             const void* v_base, size_t slot_stride, int grid, bool cooperative,
+                             cudaStream_t stream);
+int flash_pair_max_grid();  // CTAs (an even number) of the pairs resident at once
+
 // Merge the split partials (nsplit > 1: every unit; balanced: the units a CTA
 // boundary cuts) into the final output (and LSE), or into acc/m/l when partial.
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream);
@@ -171,7 +181,8 @@ struct FlashArgs {
 };
 
 struct FlashPlan {
-  int rows_per_unit;  // 128 (one query tile per CTA) or 256 (two-tile bf16 kernel)
+  int rows_per_unit;  // 128 (one query tile per CTA), 256 (two-tile bf16 kernel) or
+                      // 512 (bf16 d=128 kernel on CTA pairs)
   int nsplit;         // equal-split chunks per unit; 1 under the balanced schedule
   int balanced;       // 1: balanced schedule (n_items == grid == CTAs)
   int full_waves;     // balanced: whole-unit waves before the shared-out remainder

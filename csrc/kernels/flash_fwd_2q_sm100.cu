@@ -357,12 +357,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-        int lim = kN;  // visible columns: c <= lim
+        int lim = kN;   // visible columns: c <= lim
+        int cls = 1;    // this query tile's class of the tile: 0 masked, 1 full, 2 diagonal
         if constexpr (kCausal) {
           if (!visible2(p, it.q0, &v, tpb)) continue;
           int k_lo = 0, q_lo = 0;
           int vq = v;  // this query tile's own classification; v itself is visible to the unit
-          const int cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
+          cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
           lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);
         }
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], g & 1, st, kSiteSFull, tmo));
@@ -373,18 +374,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
         for (int c = 0; c < kN; c += 32) tmem_ld32(s_col + c, sr + c);
         tmem_ld_wait();
-        if constexpr (kCausal) {
+        if (kCausal && cls != 1) {
+          // only tiles the mask cuts (the same class for every row of the query
+          // tile, so the branch is uniform); full tiles skip the 128 selects
 #pragma unroll
           for (int c = 0; c < kN; ++c)
             if (c > lim) sr[c] = 0xff800000u;  // -inf
         }
+        // row max: 3-input max folds two new columns per instruction
         float pm[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sr[i]);
 #pragma unroll
-        for (int c = 8; c < kN; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
-        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * sl2;
+        for (int c = 8; c < kN; c += 2)
+          pm[(c >> 1) & 7] =
+              fmax3(pm[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        const float mx = fmaxf(fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                                     pm[6]),
+                               pm[7]) * sl2;
         const bool need = mx > m_run + kRescaleThreshold;
         float alpha = 1.f;
         if (need) {
@@ -409,19 +416,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        // exponentials, row sum, packed bf16 P over the first 64 S columns
-        float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // exponentials, row sum, packed bf16 P over the first 64 S columns;
+        // the scale-and-shift and the row sum run as packed fp32 pairs
+        const float2 scale2 = make_float2(sl2, sl2);
+        const float2 shift2 = make_float2(-m_use, -m_use);
+        float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
         uint32_t pk[kN / 2];
 #pragma unroll
         for (int i = 0; i < kN / 2; ++i) {
-          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, -m_use));
-          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, -m_use));
-          ps8[i & 7] += e0 + e1;
-          pk[i] = pack_bf16x2(e0, e1);
+          const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]),
+                                             __uint_as_float(sr[2 * i + 1])),
+                                 scale2, shift2);
+          const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          ps2[i & 3] = fadd2(ps2[i & 3], e);
+          pk[i] = pack_bf16x2(e.x, e.y);
         }
 #pragma unroll
         for (int c = 0; c < kN / 2; c += 32) tmem_st32(s_col + c, pk + c);
-        l_run += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+        const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
+        l_run += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[x]);

@@ -59,6 +59,16 @@ bool use_two_tile(const FlashArgs& a, int sms) {
          static_cast<long long>(a.Hq) * (a.Sq / 256) >= 2LL * sms;
 }
 
+// CTA-pair kernel (bf16, d = 128, 512-row units): RAB_FLASH_2SM=1 selects it
+// where the shape allows it (and =0 never does).
+bool use_pair(const FlashArgs& a) {
+  if (a.prec != Prec::kBF16 || a.D != 128 || a.Sq % 512 != 0 || a.Skv % 128 != 0) return false;
+  if (a.causal && a.zigzag && (a.Sq / 2) % 512 != 0) return false;
+  if (a.nsplit < 0) return false;  // the balanced schedule is one-tile only
+  const char* e = std::getenv("RAB_FLASH_2SM");
+  return e != nullptr && std::strcmp(e, "1") == 0;
+}
+
 // Visible KV tiles of the 128-row query tile at local row q0, as ranges of
 // ring tile indices: keys grow along each contiguous chunk of a ring block
 // (the whole block, or each half under zigzag), so each chunk contributes the
@@ -154,9 +164,13 @@ std::vector<std::pair<int, int>> flash_visible_ranges(const FlashArgs& a, int q0
 FlashPlan flash_plan(const FlashArgs& a) {
   if (a.Sq <= 0 || a.Sq % 128 != 0) throw std::runtime_error("flash: Sq must be a positive multiple of 128");
   FlashPlan pl{};
-  const int sms = a.sms > 0 ? a.sms : flash_sm_count();
+  const int sm_total = a.sms > 0 ? a.sms : flash_sm_count();
+  const bool pair = use_pair(a);
+  // the pair kernel's workers are CTA pairs (as many as are resident at once)
+  const int pair_grid = pair ? (a.sms > 0 ? (a.sms / 2) * 2 : flash_pair_max_grid()) : 0;
+  const int sms = pair ? pair_grid / 2 : sm_total;
   // bf16 may use the two-query-tile kernel when the rows split into 256-row units
-  pl.rows_per_unit = use_two_tile(a, sms) ? 256 : 128;
+  pl.rows_per_unit = pair ? 512 : (use_two_tile(a, sms) ? 256 : 128);
   pl.n_units = a.Hq * (a.Sq / pl.rows_per_unit);
   const int tiles = tiles_of(a);
   // per-item overhead in tiles: ~6 of the fp32 kernel's 64-key tiles, ~3 of 128-key bf16 tiles
@@ -190,6 +204,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.n_items = pl.n_units * pl.nsplit;
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
   if (a.fused) pl.grid = a.grid > 0 ? a.grid : sms;  // every CTA also copies a slice
+  if (pair) pl.grid = 2 * (a.fused ? sms : std::min(pl.n_items, sms));  // two CTAs per worker
   pl.workspace_bytes = pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * pl.rows_per_unit *
                                            (a.D + 2) * sizeof(float)
                                      : 0;
@@ -259,7 +274,11 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   const FlashMaps& maps =
       cached_maps(a.prec, a.k_base, a.v_base, a.slot_stride, a.nblk, a.Skv, a.Hkv, a.D);
   int err;
-  if (pl.rows_per_unit == 256) {
+  if (pl.rows_per_unit == 512) {
+    const CUtensorMap tq = flash_make_q_map(a.q, a.Sq, a.Hq, a.D);
+    err = flash_forward_2sm_launch(p, tq, a.k_base, a.v_base, a.slot_stride, pl.grid, a.fused,
+                                   stream);
+  } else if (pl.rows_per_unit == 256) {
     const CUtensorMap tq = flash_make_q_map(a.q, a.Sq, a.Hq, a.D);
     err = flash_forward_2q_launch(p, tq, maps, pl.grid, a.fused, stream);
   } else {
