@@ -355,6 +355,9 @@ def main() -> int:
              "rows_per_rank": 256, "heads": "all",
              "oracle": "float64 over all ranks' K/V regenerated from their seeds (max over ranks)"}
 
+    # ---- overlap trace of one extra call (outside the timed regions) ----
+    overlap = attn.overlap_trace(q, k, v, out=out) if world > 1 else None
+
     nsplit = attn.engine.nsplit
     # ring-format prep (fp32, one launch), the fused kernel, the merge pass (split or balanced)
     per_step = (1 if dt == "fp32" else 0) + 1 + (1 if nsplit != 1 else 0)
@@ -386,6 +389,7 @@ def main() -> int:
                               f"{'rank' if seed is None else f'{seed}+rank'}, "
                               f"scale 1/sqrt({head_dim})"),
                 "check": check,
+                "overlap": overlap,
                 "l2": "256 MiB buffer written between timed steps (outside the events)",
                 "host_affinity": host_affinity,
                 "flops_per_step_total": flops_total,

@@ -99,6 +99,12 @@ class FusedRing {
   int nsplit() const { return plan_.balanced ? -1 : plan_.nsplit; }  // -1: balanced schedule
   const FlashArgs& args() const { return args_; }  // shapes and precision of the engine
   uint64_t launches() const { return epoch_; }
+  // Overlap trace of the following launches (FlashParams::stamps), one
+  // [grid][kMaxSlots][2] globaltimer record per launch, cleared before each.
+  void set_trace(bool on);
+  // copy of the last traced launch's stamps into host memory of trace_words() uint64
+  void read_trace(uint64_t* host) const;
+  size_t trace_words() const { return static_cast<size_t>(plan_.grid) * kMaxSlots * 2; }
 
  private:
   RingContext& ctx_;
@@ -107,6 +113,8 @@ class FusedRing {
   size_t slots_off_ = 0;
   size_t slot_bytes_ = 0;
   void* workspace_ = nullptr;
+  uint64_t* stamps_ = nullptr;
+  bool trace_ = false;
   uint64_t epoch_ = 0;
   uint64_t arrive_total_ = 0;
   uint64_t reads_total_ = 0;

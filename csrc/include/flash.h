@@ -80,6 +80,10 @@ struct FlashParams {
   // ---- diagnostics ----
   DeviceStatus* status;
   uint64_t timeout_ns;
+  // optional overlap trace, [grid][kMaxSlots][2] globaltimer ns per CTA:
+  // [c][0] = (TMA role start, TMA role end), [c][s] = (first wait for ring
+  // block s, block s present); nullptr: off
+  uint64_t* stamps;
 };
 
 // Host side: tensor maps for the K/V slots.  For kBF16 the slots hold K and V
@@ -178,6 +182,7 @@ struct FlashArgs {
   uint64_t epoch = 0;
   uint64_t arrive_target = 0;
   uint64_t reads_target = 0;
+  uint64_t* stamps = nullptr;        // optional overlap trace (FlashParams::stamps)
 };
 
 struct FlashPlan {

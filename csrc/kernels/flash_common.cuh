@@ -210,6 +210,26 @@ __device__ __forceinline__ bool wait_flag(const uint64_t* flag, uint64_t target,
   }
 }
 
+// Overlap trace (p.stamps != nullptr): see FlashParams::stamps.
+__device__ __forceinline__ void trace_stamp(const FlashParams& p, int slot, int which,
+                                            uint64_t t) {
+  if (p.stamps != nullptr)
+    p.stamps[(static_cast<size_t>(blockIdx.x) * kMaxSlots + slot) * 2 + which] = t;
+}
+
+// The TMA thread's wait for ring block s to be present locally (fused mode),
+// with the overlap trace.
+__device__ __forceinline__ bool wait_block(const FlashParams& p, int s) {
+  const uint64_t t0 = p.stamps != nullptr ? globaltimer_ns() : 0;
+  const bool ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false,
+                            p.status, kSiteBlockReady, s, p.timeout_ns);
+  if (p.stamps != nullptr) {
+    trace_stamp(p, s, 0, t0);
+    trace_stamp(p, s, 1, globaltimer_ns());
+  }
+  return ok;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      trace_stamp(p, 0, 0, globaltimer_ns());
       int g = 0, item_count = 0, ready_blocks = 1;
       bool ok = true;
       for (int w = 0; ok; ++w, ++item_count) {
@@ -209,8 +210,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
-            ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
-                           kSiteBlockReady, s, tmo);
+            ok = wait_block(p, s);
             if (!ok) break;
             fence_proxy_async_global();
             ready_blocks = s + 1;
@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           ++g;
         }
       }
+      trace_stamp(p, 0, 1, globaltimer_ns());
       if (!ok) {
         for (int i = 0; i < NS && i < g; ++i) {
           const int gg = g - 1 - i;

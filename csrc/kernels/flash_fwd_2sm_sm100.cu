@@ -193,6 +193,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+        trace_stamp(p, 0, 0, globaltimer_ns());
         int g = 0, item_count = 0, ready_blocks = 1;
         bool ok = true;
         for (int w = 0; ok; ++w, ++item_count) {
@@ -248,8 +249,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             }
             const int s = v / tpb, t = v - s * tpb;
             if (p.fused && s >= ready_blocks) {
-              ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
-                             kSiteBlockReady, s, tmo);
+              ok = wait_block(p, s);
               if (!ok) break;
               fence_proxy_async_global();
               ready_blocks = s + 1;
@@ -273,6 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             ++g;
           }
         }
+        trace_stamp(p, 0, 1, globaltimer_ns());
         if (!ok) {
           // drain this CTA's own loads (their barriers are local)
           for (int i = 0; i < kStages && i < g; ++i) {

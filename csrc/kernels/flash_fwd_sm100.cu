@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      trace_stamp(p, 0, 0, globaltimer_ns());
       int g = 0;
       int ready_blocks = 1;  // blocks [0, ready_blocks) known present locally
       bool ok = true;
@@ -213,8 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
-            ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false, st,
-                           kSiteBlockReady, s, tmo);
+            ok = wait_block(p, s);
             if (!ok) break;
             fence_proxy_async_global();
             ready_blocks = s + 1;
@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++g;
         }
       }
+      trace_stamp(p, 0, 1, globaltimer_ns());
       if (!ok) {
         // drain the loads this thread issued before giving up
         for (int i = 0; i < NS && i < g; ++i) {

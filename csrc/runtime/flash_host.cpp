@@ -270,6 +270,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.reads_target = a.reads_target;
   p.status = a.status;
   p.timeout_ns = static_cast<uint64_t>(a.timeout_s * 1e9);
+  p.stamps = a.stamps;
   if (p.status == nullptr) throw std::runtime_error("flash: a device status word is required");
   const FlashMaps& maps =
       cached_maps(a.prec, a.k_base, a.v_base, a.slot_stride, a.nblk, a.Skv, a.Hkv, a.D);

@@ -63,6 +63,19 @@ FusedRing::FusedRing(RingContext& ctx, Prec prec, int seq, int heads, int heads_
 
 FusedRing::~FusedRing() {
   if (workspace_) cudaFree(workspace_);
+  if (stamps_) cudaFree(stamps_);
+}
+
+void FusedRing::set_trace(bool on) {
+  if (on && stamps_ == nullptr)
+    cuda_check(cudaMalloc(&stamps_, trace_words() * sizeof(uint64_t)), "cudaMalloc(trace)");
+  trace_ = on;
+}
+
+void FusedRing::read_trace(uint64_t* host) const {
+  if (stamps_ == nullptr) throw std::runtime_error("FusedRing: tracing was never enabled");
+  cuda_check(cudaMemcpy(host, stamps_, trace_words() * sizeof(uint64_t), cudaMemcpyDeviceToHost),
+             "read trace");
 }
 
 uint8_t* FusedRing::slot0_k() const { return ctx_.local(slots_off_); }
@@ -94,6 +107,11 @@ void FusedRing::attend(const void* q, void* out, bool out_bf16, float* lse, floa
     a.epoch = epoch_;
     a.arrive_target = arrive_total_;
     a.reads_target = reads_total_;
+  }
+  if (trace_) {
+    cuda_check(cudaMemsetAsync(stamps_, 0, trace_words() * sizeof(uint64_t), stream),
+               "clear trace");
+    a.stamps = stamps_;
   }
   const int err = flash_run(a, plan_, stream);
   cuda_check(static_cast<cudaError_t>(err), "fused ring attention launch");

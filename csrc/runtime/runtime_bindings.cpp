@@ -274,6 +274,14 @@ void register_runtime(py::module_& m) {
            },
            py::arg("q"), py::arg("out"), py::arg("lse") = c10::nullopt, py::arg("scale"))
       .def("check", &FusedRing::check)
+      .def("set_trace", &FusedRing::set_trace)
+      .def("read_trace",
+           [](const FusedRing& f) {
+             torch::Tensor t = torch::empty({static_cast<int64_t>(f.grid()), kMaxSlots, 2},
+                                            torch::dtype(torch::kInt64));
+             f.read_trace(reinterpret_cast<uint64_t*>(t.data_ptr()));
+             return t;
+           })
       .def_property_readonly("grid", &FusedRing::grid)
       .def_property_readonly("nsplit", &FusedRing::nsplit)
       .def_property_readonly("launches", &FusedRing::launches)

@@ -118,6 +118,23 @@ class RingAttention:
     def check(self) -> None:
         self.engine.check()
 
+    def overlap_trace(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      out: Optional[torch.Tensor] = None) -> dict:
+        """One call with the kernel's overlap trace on (per CTA: when each ring
+        block was first waited for and when it was present); returns the
+        summary of `utils.overlap.summarize`.  Synchronises; every rank of the
+        job must call it together, like any other call."""
+        from ..utils.overlap import summarize
+
+        self.engine.set_trace(True)
+        try:
+            self(q, k, v, out=out, check=True)
+            torch.cuda.synchronize(q.device)
+            stamps = self.engine.read_trace()
+        finally:
+            self.engine.set_trace(False)
+        return summarize(stamps, self.world)
+
     def close(self) -> None:
         self.engine = None
         if self._own_runtime and self.runtime is not None:

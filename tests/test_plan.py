@@ -108,3 +108,26 @@ def test_plan_forced_modes(C, monkeypatch):
     assert pl["balanced"] == 0 and pl["nsplit"] == 3 and pl["n_items"] == 768
     with pytest.raises(RuntimeError, match="balanced"):
         C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, causal=True, nsplit=-1, sms=148)
+
+
+def test_pair_kernel_plan(monkeypatch):
+    """RAB_FLASH_2SM=1 selects the CTA-pair kernel (512-row units, an even grid
+    of pairs) for bf16 d=128 shapes that split into 512-row units, and nothing
+    else."""
+    from ring_attention_benchmark_b200 import _ext
+
+    C = _ext.load()
+    monkeypatch.setenv("RAB_FLASH_2SM", "1")
+    info = C.flash_plan_info(0, 4096, 4096, 2, 8, 8, 128, causal=True, zigzag=True, world=2,
+                             rank=0, sms=148)
+    assert info["rows_per_unit"] == 512 and info["grid"] % 2 == 0 and info["grid"] <= 148
+    assert info["dynamic"] == 1
+    fused = C.flash_plan_info(0, 4096, 4096, 2, 8, 8, 128, world=2, sms=148, fused=True)
+    assert fused["rows_per_unit"] == 512 and fused["grid"] == 148
+    # d=64, fp32, a zigzag half that is not a multiple of 512 rows: not the pair kernel
+    assert C.flash_plan_info(0, 4096, 4096, 1, 8, 8, 64, sms=148)["rows_per_unit"] != 512
+    assert C.flash_plan_info(1, 4096, 4096, 1, 1, 1, 64, sms=148)["rows_per_unit"] == 128
+    assert C.flash_plan_info(0, 1536, 1536, 2, 8, 8, 128, causal=True, zigzag=True, world=2,
+                             sms=148)["rows_per_unit"] != 512
+    monkeypatch.setenv("RAB_FLASH_2SM", "0")
+    assert C.flash_plan_info(0, 4096, 4096, 1, 8, 8, 128, sms=148)["rows_per_unit"] != 512
