@@ -132,7 +132,9 @@ def reference_arm(args) -> int:
                 tail = (out.strip().splitlines() or err.strip().splitlines() or ["no output"])
                 first_fail = first_fail or f"{b}: exit {rc}: {tail[-1].strip()}"
             else:
-                per_backend[b] = {"avg_total_ms": ms, "summary": out.strip().splitlines()[-2:]}
+                lines = out.strip().splitlines()
+                per_backend[b] = {"avg_total_ms": ms, "summary": [
+                    l.strip() for l in lines if " bench:" in l or l.startswith("avg_total=")]}
     clocks = sampler.stop() if rank == 0 else None
     if rank != 0:
         return 0

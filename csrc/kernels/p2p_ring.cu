@@ -4,11 +4,12 @@
 // Same data movement as the reference loops (src/loop/ring_loop_*.cu: every
 // step sends the current shard to rank+1 and receives the next one from
 // rank-1, two buffers swapped per step) but with no library call.  The shard
-// is cut into chunks dealt round-robin to the CTAs (CTA c of G owns chunks c,
-// c+G, c+2G, ...: at any moment the G CTAs write neighbouring addresses, which
-// measured ~5 % faster over NVLink on B200 than one contiguous slice per
-// CTA).  Each CTA pushes its chunks into the right neighbour's receive buffer
-// and hands over with two monotonically increasing flags per CTA:
+// is cut into 8 KiB chunks dealt round-robin to the CTAs (CTA c of G owns
+// chunks c, c+G, c+2G, ...: at any moment the G CTAs write neighbouring
+// addresses, which measured ~5 % faster over NVLink on B200 than one
+// contiguous slice per CTA, and no CTA holds more than one chunk over
+// another).  Each CTA pushes its chunks into the right neighbour's receive
+// buffer and hands over with two monotonically increasing flags per CTA:
 //   arrived[c] (in the receiver's memory)  step n of CTA c's chunks has landed
 //   sent[c]    (in the sender's memory)    the sender finished reading them
 // so each CTA runs its own pipeline and no grid-wide barrier is needed.  All
@@ -55,8 +56,8 @@ __device__ bool wait_ge(const uint64_t* flag, uint64_t target, DeviceStatus* st,
 }
 
 constexpr int kVecThreads = 512;
-constexpr int kVecUnroll = 4;
-constexpr size_t kVecChunk16 = static_cast<size_t>(kVecThreads) * kVecUnroll;  // 32 KiB
+constexpr int kVecUnroll = 4;                                   // chunks in flight per thread
+constexpr size_t kVecChunk16 = static_cast<size_t>(kVecThreads);  // 8 KiB chunks
 
 __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyParams p) {
   const int c = blockIdx.x;
@@ -76,17 +77,20 @@ __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyPar
     if (!s_ok) return;
     const uint4* src = reinterpret_cast<const uint4*>(p.buf[sg & 1]);
     uint4* dst = reinterpret_cast<uint4*>(p.right_buf[(sg + 1) & 1]);
-    for (size_t base = kVecChunk16 * c; base < n16; base += stride16) {
+    // chunks c, c + G, c + 2G, ... of 8 KiB (one 16-byte vector per thread),
+    // kVecUnroll of them in flight; the CTAs' shares differ by one chunk at most
+    size_t base = kVecChunk16 * c;
+    for (; base + (kVecUnroll - 1) * stride16 + kVecChunk16 <= n16; base += kVecUnroll * stride16) {
       const size_t i = base + threadIdx.x;
-      if (base + kVecChunk16 <= n16) {
-        uint4 r[kVecUnroll];
+      uint4 r[kVecUnroll];
 #pragma unroll
-        for (int u = 0; u < kVecUnroll; ++u) r[u] = __ldcg(src + i + u * kVecThreads);
+      for (int u = 0; u < kVecUnroll; ++u) r[u] = __ldcg(src + i + u * stride16);
 #pragma unroll
-        for (int u = 0; u < kVecUnroll; ++u) dst[i + u * kVecThreads] = r[u];
-      } else {
-        for (size_t j = i; j < n16; j += kVecThreads) dst[j] = __ldcg(src + j);
-      }
+      for (int u = 0; u < kVecUnroll; ++u) dst[i + u * stride16] = r[u];
+    }
+    for (; base < n16; base += stride16) {
+      const size_t i = base + threadIdx.x;
+      if (i < n16) dst[i] = __ldcg(src + i);
     }
     // The barrier orders every thread's stores before thread 0's system-scope
     // release, and release is cumulative, so the neighbour that acquires
