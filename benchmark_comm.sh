@@ -6,7 +6,8 @@
 # (local | torchrun | mpirun | srun | none) MPIRUN HOSTFILE MPIRUN_EXTRA_ARGS SRUN
 # SRUN_MPI_TYPE SRUN_EXTRA_ARGS.  SIZES overrides COMM_SIZES; SIZE_UNIT=elements reads
 # the sizes as fp32 element counts (default bytes).  RESUME=1 with
-# RAB_RESULTS_JSONL skips configurations that file already records.  Stops at the first
+# RAB_RESULTS_JSONL skips configurations that file already records.  INPROCESS=1 runs
+# every (backend, size) in one launch of the ranks.  Stops at the first
 # failing backend/size, like the reference wrapper.
 set -euo pipefail
 
@@ -42,6 +43,21 @@ echo "launcher=${LAUNCHER} np=${NP} warmup=${WARMUP} iters=${ITERS}"
 echo "sizes=${SIZES} (${SIZE_UNIT:-bytes})"
 echo "backends=${BACKENDS}"
 echo ""
+
+# INPROCESS=1: every (backend, size) in one launch of the ranks (one runtime
+# set-up per job instead of one per run); the output lines are the same.
+if [[ "${INPROCESS:-0}" == "1" ]]; then
+  byte_list=""
+  for size in ${SIZES}; do byte_list="${byte_list:+${byte_list},}$(size_to_bytes "${size}")"; done
+  if ! launch_ranks "${NP}" -m ring_attention_benchmark_b200.cli sweep comm "${WARMUP}" "${ITERS}" \
+      "${byte_list}" "$(echo ${BACKENDS} | tr ' ' ',')"; then
+    echo "ERROR: in-process sweep failed"
+    exit 1
+  fi
+  echo "========== Done =========="
+  echo "Finished at: $(date)"
+  exit 0
+fi
 
 for backend in ${BACKENDS}; do
   exe="${BIN_DIR}/ring_loop_${backend}"

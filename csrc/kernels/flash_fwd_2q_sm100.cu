@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     mbar_init(q_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
-      mbar_init(&p_full[x], 128);
+      mbar_init(&p_full[x], 4);  // one arrival per softmax warp
       mbar_init(&pv_done[x], 1);
     }
     mbar_init(o_final, 1);
@@ -439,7 +439,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
         l_run += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_full[x]);
+        __syncwarp();  // the warp's TMEM stores are complete and fenced
+        if (lane_id() == 0) mbar_arrive(&p_full[x]);
         ++j;
         ++g;
       }

@@ -29,7 +29,7 @@
 //    CTA drains its own loads on an error;
 //  * the MMA's completions (S ready, stage free, PV done, O final, Q free)
 //    are committed to the same barrier in both CTAs (multicast commit);
-//  * both CTAs' softmax threads arrive on the leader's P-ready barriers;
+//  * both CTAs' softmax warps arrive on the leader's P-ready barriers;
 //  * causal launches claim work items dynamically in the leader's TMA thread,
 //    which writes each item into both CTAs' shared-memory queues.
 // Every wait is bounded; the pair unwinds together and meets at a cluster
@@ -144,7 +144,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
     mbar_init(q_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
-      mbar_init(&p_full[x], 256);  // 128 softmax threads of each CTA
+      mbar_init(&p_full[x], 8);  // one arrival per softmax warp of each CTA
       mbar_init(&pv_done[x], 1);
     }
     mbar_init(o_final, 1);
@@ -513,10 +513,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         l_run += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
-        if (leader)
-          mbar_arrive(&p_full[x]);
-        else
-          mbar_arrive_cluster(p_bar);
+        __syncwarp();  // the warp's TMEM stores are complete and fenced
+        if (lane_id() == 0) {
+          if (leader)
+            mbar_arrive(&p_full[x]);
+          else
+            mbar_arrive_cluster(p_bar);
+        }
         ++j;
         ++g;
       }

@@ -147,10 +147,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(&p_full[0], 256);
-    mbar_init(&p_full[1], 256);
+    mbar_init(&p_full[0], 8);  // one arrival per softmax warp
+    mbar_init(&p_full[1], 8);
     mbar_init(pv_done, 1);
-    mbar_init(q_full, 256);
+    mbar_init(q_full, 8);
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
@@ -455,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(q_full);
+        __syncwarp();  // the warp's TMEM stores are complete and fenced
+        if (lane == 0) mbar_arrive(q_full);
       }
       float m_run = -INFINITY;  // running max of scaled log2 scores (same in both halves)
       float l_part = 0.f;       // this half's share of the row sum
@@ -556,7 +557,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_full[b]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[b]);
         ++j;
         ++g;
       }

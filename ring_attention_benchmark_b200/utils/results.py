@@ -19,7 +19,7 @@ from __future__ import annotations
 import json
 import os
 import time
-from typing import Dict, Optional
+from typing import List, Dict, Optional
 
 COMM_LABEL = {
     "staged": "staged",
@@ -131,6 +131,48 @@ def has_record(path: str, **match) -> bool:
     return False
 
 
+def load_records(path: str) -> List[Dict]:
+    out = []
+    with open(path) as f:
+        for line in f:
+            try:
+                out.append(json.loads(line))
+            except ValueError:
+                continue
+    return out
+
+
+def sweep_table(records: List[Dict], kind: str) -> str:
+    """Markdown table of a sweep's records: one row per (ranks, backend), one
+    column per size.  comm: total GB/s ((np-1) * bytes / avg_total); attention:
+    avg_total ms and TFLOP/s.  The last record of a configuration wins."""
+    cells: Dict = {}
+    sizes, rows = set(), []
+    for r in records:
+        if r.get("kind") != kind:
+            continue
+        key = (r["ranks"], r["backend"])
+        if key not in rows:
+            rows.append(key)
+        sizes.add(r["bytes"])
+        total = r["avg_ms"].get("total", 0.0)
+        if kind == "comm":
+            g = gbps((r["ranks"] - 1) * r["bytes"], total)
+            cells[key + (r["bytes"],)] = "n/a" if g is None else f"{g:.1f}"
+        else:
+            cells[key + (r["bytes"],)] = f"{total:.3f} ms / {r.get('tflops', 0.0):.2f}"
+    cols = sorted(sizes)
+    unit = "bytes" if kind == "comm" else "bytes (tokens/rank = bytes/256)"
+    head = "| np | backend | " + " | ".join(str(c) for c in cols) + " |"
+    lines = [f"({kind}; columns: shard size in {unit}; cells: "
+             + ("total GB/s" if kind == "comm" else "avg_total ms / TFLOP/s") + ")", "",
+             head, "|" + "---|" * (len(cols) + 2)]
+    for key in sorted(rows, key=lambda k: (k[0], rows.index(k))):
+        lines.append(f"| {key[0]} | {key[1]} | " +
+                     " | ".join(cells.get(key + (c,), "") for c in cols) + " |")
+    return "\n".join(lines)
+
+
 def main(argv=None) -> int:
     """``python -m ring_attention_benchmark_b200.utils.results has --kind comm
     --backend B --bytes N --ranks R --warmup W --iters I [--prec P --data D]``:
@@ -147,7 +189,13 @@ def main(argv=None) -> int:
         h.add_argument("--" + k, type=int, required=True)
     h.add_argument("--prec")
     h.add_argument("--data")
+    t = sub.add_parser("table")
+    t.add_argument("path")
+    t.add_argument("--kind", required=True, choices=("comm", "attention"))
     a = ap.parse_args(argv)
+    if a.cmd == "table":
+        print(sweep_table(load_records(a.path), a.kind))
+        return 0
     match = {"kind": a.kind, "backend": a.backend, "bytes": a.bytes, "ranks": a.ranks,
              "warmup": a.warmup, "iters": a.iters}
     if a.prec:

@@ -6,6 +6,7 @@ import json
 import os
 import re
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -199,3 +200,30 @@ def test_resume_skips_recorded_configurations(tmp_path):
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "SKIP backend=staged kv_size=4096" in r.stdout and "--- kv_size" not in r.stdout
+
+
+def test_sweep_table_from_jsonl():
+    """`results table` turns a sweep's JSONL records into one markdown row per
+    (ranks, backend) and one column per size."""
+    from ring_attention_benchmark_b200.utils.results import sweep_table
+
+    recs = [{"kind": "comm", "backend": "nccl", "bytes": 1 << 20, "ranks": 2,
+             "avg_ms": {"total": 0.01}},
+            {"kind": "comm", "backend": "b200_fused", "bytes": 1 << 20, "ranks": 2,
+             "avg_ms": {"total": 0.005}},
+            {"kind": "comm", "backend": "nccl", "bytes": 1 << 24, "ranks": 4,
+             "avg_ms": {"total": 0.1}},
+            {"kind": "attention", "backend": "nccl", "bytes": 262144, "ranks": 2,
+             "avg_ms": {"total": 0.5}, "tflops": 1.2}]
+    t = sweep_table(recs, "comm").splitlines()
+    assert "| np | backend | 1048576 | 16777216 |" in t
+    assert "| 2 | b200_fused | 209.7 |  |" in t
+    assert "| 4 | nccl |  | 503.3 |" in t
+    assert "| 2 | nccl | 0.500 ms / 1.20 |" in sweep_table(recs, "attention")
+
+
+def test_sweep_program_rejects_bad_arguments():
+    r = subprocess.run([sys.executable, "-m", "ring_attention_benchmark_b200.cli", "sweep",
+                        "attention", "1", "1", "100", "nccl"], cwd=ROOT, capture_output=True,
+                       text=True)
+    assert r.returncode == 1 and "bad arguments" in r.stdout

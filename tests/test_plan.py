@@ -82,10 +82,18 @@ def test_plan_many_heads_two_tile(C, monkeypatch):
     pl = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, sms=148)
     assert pl["rows_per_unit"] == 128 and pl["nsplit"] == 1 and pl["n_items"] == 4096
     monkeypatch.delenv("RAB_FLASH_2Q")
-    # too few 256-row units (64 < 2 waves): one-tile kernel; causal: one-tile kernel
+    # too few non-causal 256-row units (64 < 2 waves): one-tile kernel; causal: the
+    # two-tile kernel with dynamic claiming, whatever the size
     assert C.flash_plan_info(BF16, 16384, 16384, 1, 1, 1, 128, sms=148)["rows_per_unit"] == 128
-    assert C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True,
+    pc = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True, sms=148)
+    assert pc["rows_per_unit"] == 256 and pc["dynamic"] == 1
+    assert C.flash_plan_info(BF16, 1024, 1024, 1, 1, 1, 128, causal=True,
+                             sms=148)["rows_per_unit"] == 256
+    # the balanced schedule is never combined with the two-tile kernel, even when forced
+    monkeypatch.setenv("RAB_FLASH_2Q", "1")
+    assert C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=-1,
                              sms=148)["rows_per_unit"] == 128
+    monkeypatch.delenv("RAB_FLASH_2Q")
     # fp32 never
     assert C.flash_plan_info(F32, 16384, 16384, 1, 32, 32, 64, sms=148)["rows_per_unit"] == 128
 
