@@ -176,6 +176,61 @@ __device__ __forceinline__ int classify(const FlashParams& p, int q0, int* v_io,
   return 2;
 }
 
+// Causal walk over the KV tiles [v_begin, v_end) of a work item that a query
+// range ending at global position q_hi can see, in ring order, with the first
+// global key position of each tile.  Keys grow along each contiguous chunk of
+// a ring block (the whole block, or each half under zigzag sharding), so the
+// visible tiles of a chunk are a prefix of it: the walk steps tile by tile
+// with one compare and jumps to the next chunk at the first masked tile.  The
+// owner of a block (a modulo) is computed once per block, not per tile.
+// Every role of a CTA walks the same sequence.
+template <int kN>
+struct TileWalk {
+  int v, v_end;   // current tile (ring tile index) and end of the range
+  int k_lo;       // first global key position of tile v
+  int t;          // tile within its block
+  int chunk_end;  // tile (within the block) where the current chunk ends
+  int tpb, q_hi;
+
+  // position the walk at tile `v_new` (no visibility check)
+  __device__ __forceinline__ void seek(const FlashParams& p, int v_new) {
+    v = v_new;
+    if (v >= v_end) return;
+    const int s = v / tpb;
+    t = v - s * tpb;
+    const int tpc = p.zigzag ? tpb / 2 : tpb;
+    const int c = t >= tpc ? 1 : 0;
+    const int owner = ((p.rank - p.blk_offset - s) % p.world + p.world) % p.world;
+    k_lo = global_pos(c * tpc * kN, owner, p.Skv, p.world, p.zigzag) + (t - c * tpc) * kN;
+    chunk_end = (c + 1) * tpc;
+  }
+  // skip masked tiles from the current one (the rest of their chunk); false
+  // at the end of the range
+  __device__ __forceinline__ bool settle(const FlashParams& p) {
+    while (v < v_end && k_lo > q_hi) seek(p, v - t + chunk_end);
+    return v < v_end;
+  }
+  __device__ __forceinline__ bool begin(const FlashParams& p, int v_begin, int v_end_, int tpb_,
+                                        int q_hi_) {
+    v_end = v_end_;
+    tpb = tpb_;
+    q_hi = q_hi_;
+    seek(p, v_begin);
+    return settle(p);
+  }
+  // advance to the next visible tile; false at the end of the range
+  __device__ __forceinline__ bool next(const FlashParams& p) {
+    ++v;
+    ++t;
+    if (v >= v_end) return false;
+    if (t == chunk_end)
+      seek(p, v);  // next chunk or next block
+    else
+      k_lo += kN;
+    return settle(p);
+  }
+};
+
 __device__ __forceinline__ uint64_t ld_acquire_gpu(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -75,14 +75,12 @@ struct Cfg2 {
 __device__ __forceinline__ uint32_t col_s(int x) { return x ? 128u : 0u; }
 __device__ __forceinline__ uint32_t col_o(int x) { return x ? 384u : 256u; }
 
-// A KV tile is processed when it is visible to either query tile of the unit.
-// When it is not, *v_io moves to the end of the masked run (masked for the
-// second, later query tile means masked for both).
-__device__ __forceinline__ bool visible2(const FlashParams& p, int q0, int* v_io, int tpb) {
-  int a, b;
-  int v1 = *v_io;
-  if (classify(p, q0, &v1, 128, tpb, &a, &b) != 0) return true;
-  return classify(p, q0 + kM, v_io, 128, tpb, &a, &b) != 0;
+// Last global query position of the 256-row unit at local row q0: a KV tile is
+// processed when either query tile sees it, i.e. when the later tile's last
+// row does (positions grow along each chunk of the rank's rows, and the second
+// zigzag chunk lies after the first).
+__device__ __forceinline__ int unit_q_hi(const FlashParams& p, int q0) {
+  return global_pos(q0 + kM, p.rank, p.Sq, p.world, p.zigzag) + kM - 1;
 }
 
 // kCausal: tiles are classified against the causal mask; a non-causal
@@ -204,10 +202,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
           for (int ds = 0; ds < D / 64; ++ds)
             tma_load_3d(sQ + x * C::kQTile + ds * (kM * 128), &tmQ, q_full, ds * 64, it.h,
                         it.q0 + x * kM);
-        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if constexpr (kCausal) {
-            if (!visible2(p, it.q0, &v, tpb)) continue;
-          }
+        TileWalk<kN> wk;
+        int v = it.v_begin;
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                            : v < it.v_end;
+        for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+          if constexpr (kCausal) v = wk.v;
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_block(p, s);
@@ -296,10 +296,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
         if (!ok) break;
         tc_fence_after();
         int j = 0;
-        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if constexpr (kCausal) {
-            if (!visible2(p, it.q0, &v, tpb)) continue;
-          }
+        TileWalk<kN> wk;
+        int v = it.v_begin;
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                            : v < it.v_end;
+        for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
           const int stage = g % NS;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
           if (!ok) break;
@@ -357,15 +358,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const int qrow = q0 + row;
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int v = it.v_begin; v < it.v_end && ok; ++v) {
+      // global positions of this warpgroup's query tile (causal classification)
+      const int q_lo_own = kCausal ? global_pos(q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
+      TileWalk<kN> wk;
+      int v = it.v_begin;
+      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                          : v < it.v_end;
+      for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
         int lim = kN;   // visible columns: c <= lim
         int cls = 1;    // this query tile's class of the tile: 0 masked, 1 full, 2 diagonal
         if constexpr (kCausal) {
-          if (!visible2(p, it.q0, &v, tpb)) continue;
-          int k_lo = 0, q_lo = 0;
-          int vq = v;  // this query tile's own classification; v itself is visible to the unit
-          cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
-          lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);
+          // the tile is visible to the unit; classify it for this query tile
+          const int k_lo = wk.k_lo;
+          cls = k_lo > q_lo_own + kM - 1 ? 0 : (k_lo + kN - 1 <= q_lo_own ? 1 : 2);
+          lim = cls == 0 ? -1 : (cls == 2 ? q_lo_own + row - k_lo : kN);
         }
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], g & 1, st, kSiteSFull, tmo));
         if (!ok) break;
@@ -423,18 +429,23 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const float2 shift2 = make_float2(-m_use, -m_use);
         float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
-        uint32_t pk[kN / 2];
+        // two halves of 32 packed columns: each half's P goes to TMEM before the
+        // next is formed (fewer live registers at the softmax's 216-register cap)
 #pragma unroll
-        for (int i = 0; i < kN / 2; ++i) {
-          const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]),
-                                             __uint_as_float(sr[2 * i + 1])),
-                                 scale2, shift2);
-          const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-          ps2[i & 3] = fadd2(ps2[i & 3], e);
-          pk[i] = pack_bf16x2(e.x, e.y);
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int i = hlf * 32 + j;
+            const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]),
+                                               __uint_as_float(sr[2 * i + 1])),
+                                   scale2, shift2);
+            const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            ps2[j & 3] = fadd2(ps2[j & 3], e);
+            pk[j] = pack_bf16x2(e.x, e.y);
+          }
+          tmem_st32(s_col + hlf * 32, pk);
         }
-#pragma unroll
-        for (int c = 0; c < kN / 2; c += 32) tmem_st32(s_col + c, pk + c);
         const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
         l_run += ps.x + ps.y;
         tmem_st_wait();

@@ -497,18 +497,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
         const float2 shift2 = make_float2(-m_use, -m_use);
         float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
-        uint32_t pk[kN / 2];
+        // two halves of 32 packed columns: each half's P goes to TMEM before the
+        // next is formed (fewer live registers at the softmax's 216-register cap)
 #pragma unroll
-        for (int i = 0; i < kN / 2; ++i) {
-          const float2 xx = ffma2(make_float2(__uint_as_float(sr[2 * i]),
-                                              __uint_as_float(sr[2 * i + 1])),
-                                  scale2, shift2);
-          const float2 e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
-          ps2[i & 3] = fadd2(ps2[i & 3], e);
-          pk[i] = pack_bf16x2(e.x, e.y);
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int i = hlf * 32 + j;
+            const float2 xx = ffma2(make_float2(__uint_as_float(sr[2 * i]),
+                                               __uint_as_float(sr[2 * i + 1])),
+                                   scale2, shift2);
+            const float2 e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+            ps2[j & 3] = fadd2(ps2[j & 3], e);
+            pk[j] = pack_bf16x2(e.x, e.y);
+          }
+          tmem_st32(s_col + hlf * 32, pk);
         }
-#pragma unroll
-        for (int c = 0; c < kN / 2; c += 32) tmem_st32(s_col + c, pk + c);
         const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
         l_run += ps.x + ps.y;
         tmem_st_wait();
