@@ -88,11 +88,11 @@ constexpr uint16_t kPair = 0x3;  // multicast mask: both CTAs
 __device__ __forceinline__ uint32_t pcol_s(int x) { return x ? 128u : 0u; }
 __device__ __forceinline__ uint32_t pcol_o(int x) { return x ? 384u : 256u; }
 
-// A KV tile is processed when the unit's last 128 query rows see it: later
-// rows see more keys, so a tile masked for them is masked for all four.
-__device__ __forceinline__ bool visible_unit(const FlashParams& p, int q0, int* v_io, int tpb) {
-  int a, b;
-  return classify(p, q0 + kUnitRows - kM, v_io, kN, tpb, &a, &b) != 0;
+// Last global query position of the 512-row unit at local row q0: a KV tile is
+// processed when the unit's last 128 query rows see it (later rows see more
+// keys, so a tile masked for them is masked for all four query tiles).
+__device__ __forceinline__ int unit_q_hi(const FlashParams& p, int q0) {
+  return global_pos(q0 + kUnitRows - kM, p.rank, p.Sq, p.world, p.zigzag) + kM - 1;
 }
 
 template <bool kCausal>
@@ -243,10 +243,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             for (int ds = 0; ds < kD / 64; ++ds)
               tma_load_3d(sQ + x * kQTile + ds * (kM * 128), &tmQ, q_full, ds * 64, it.h,
                           it.q0 + x * 256 + static_cast<int>(crank) * kM);
-          for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-            if constexpr (kCausal) {
-              if (!visible_unit(p, it.q0, &v, tpb)) continue;
-            }
+          TileWalk<kN> wk;
+          int v = it.v_begin;
+          bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                              : v < it.v_end;
+          for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+            if constexpr (kCausal) v = wk.v;
             const int s = v / tpb, t = v - s * tpb;
             if (p.fused && s >= ready_blocks) {
               ok = wait_block(p, s);
@@ -338,10 +340,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             if (!ok) break;
             tc_fence_after();
             int j = 0;
-            for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-              if constexpr (kCausal) {
-                if (!visible_unit(p, it.q0, &v, tpb)) continue;
-              }
+            TileWalk<kN> wk;
+            int v = it.v_begin;
+            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                                : v < it.v_end;
+            for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
               const int stage = g % kStages;
               ok = mbar_wait_cl(&k_full[stage], (g / kStages) & 1, st, kSiteKFull, tmo);
               if (!ok) break;
@@ -389,10 +392,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             ok = mbar_wait(q_full, item_count & 1, st, kSiteQFull, tmo);
             if (!ok) break;
             mbar_arrive_cluster(leader_bar(q_full));
-            for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-              if constexpr (kCausal) {
-                if (!visible_unit(p, it.q0, &v, tpb)) continue;
-              }
+            TileWalk<kN> wk;
+            int v = it.v_begin;
+            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                                : v < it.v_end;
+            for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
               const int stage = g % kStages;
               const uint32_t ph = (g / kStages) & 1;
               ok = mbar_wait(&k_full[stage], ph, st, kSiteKFull, tmo);
@@ -438,15 +442,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
       const int qrow = q0 + row;
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int v = it.v_begin; v < it.v_end && ok; ++v) {
+      const int q_lo_own = kCausal ? global_pos(q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
+      TileWalk<kN> wk;
+      int v = it.v_begin;
+      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+                          : v < it.v_end;
+      for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
         int lim = kN;
         int cls = 1;
         if constexpr (kCausal) {
-          if (!visible_unit(p, it.q0, &v, tpb)) continue;
-          int k_lo = 0, q_lo = 0;
-          int vq = v;
-          cls = classify(p, q0, &vq, kN, tpb, &k_lo, &q_lo);
-          lim = cls == 0 ? -1 : (cls == 2 ? q_lo + row - k_lo : kN);
+          const int k_lo = wk.k_lo;  // visible to the unit; classify for this query tile
+          cls = k_lo > q_lo_own + kM - 1 ? 0 : (k_lo + kN - 1 <= q_lo_own ? 1 : 2);
+          lim = cls == 0 ? -1 : (cls == 2 ? q_lo_own + row - k_lo : kN);
         }
         ok = __all_sync(0xffffffffu, mbar_wait_cl(&s_full[x], g & 1, st, kSiteSFull, tmo));
         if (!ok) break;

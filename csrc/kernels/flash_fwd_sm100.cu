@@ -94,6 +94,11 @@ struct Cfg {
                                                   kTF32 ? kMajorK : kMajorMN);
 };
 
+// Last global query position of the 128-row query tile at local row q0.
+__device__ __forceinline__ int tile_q_hi(const FlashParams& p, int q0) {
+  return global_pos(q0, p.rank, p.Sq, p.world, p.zigzag) + kM - 1;
+}
+
 // kCausal: causal launch.  Its work items reach the MMA and softmax roles
 // through the in-CTA queue (claimed from the dynamic counter when p.dynamic,
 // else from the static list), and tiles are classified against the mask.  A
@@ -207,11 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (w >= s_work[0]) break;
           it = work_item(p, w, tiles_total, s_work);
         }
-        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if constexpr (kCausal) {
-            int k_lo, q_lo;
-            if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
-          }
+        TileWalk<kN> wk;
+        int v = it.v_begin;
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, tile_q_hi(p, it.q0))
+                            : v < it.v_end;
+        for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+          if constexpr (kCausal) v = wk.v;
           const int s = v / tpb, t = v - s * tpb;
           if (p.fused && s >= ready_blocks) {
             ok = wait_block(p, s);
@@ -329,11 +335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(pv_done);
           return true;
         };
-        for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-          if constexpr (kCausal) {
-            int k_lo, q_lo;
-            if (classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo) == 0) continue;
-          }
+        TileWalk<kN> wk;
+        int v = it.v_begin;
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, tile_q_hi(p, it.q0))
+                            : v < it.v_end;
+        for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
           const int stage = g % NS;
           const int b = g & 1;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
@@ -461,12 +467,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_run = -INFINITY;  // running max of scaled log2 scores (same in both halves)
       float l_part = 0.f;       // this half's share of the row sum
       int j = 0;
-      for (int v = it.v_begin; v < it.v_end && ok; ++v) {
-        int k_lo = 0, q_lo = 0;
+      const int q_lo = kCausal ? global_pos(it.q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
+      TileWalk<kN> wk;
+      int v = it.v_begin;
+      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, q_lo + kM - 1)
+                          : v < it.v_end;
+      for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+        int k_lo = 0;
         int cls = 1;
         if constexpr (kCausal) {
-          cls = classify(p, it.q0, &v, kN, tpb, &k_lo, &q_lo);
-          if (cls == 0) continue;  // v moved to the end of the masked run
+          // visible (the walk skips masked tiles): full or cut by the diagonal
+          k_lo = wk.k_lo;
+          cls = k_lo + kN - 1 <= q_lo ? 1 : 2;
         }
         const int b = g & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (g >> 1) & 1, st, kSiteSFull, tmo));
