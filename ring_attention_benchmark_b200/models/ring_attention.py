@@ -64,6 +64,12 @@ class RingAttention:
         self.runtime = runtime
         self.engine = C.FusedRing(runtime.ctx, prec, seq_per_rank, heads, self.heads_kv, head_dim,
                                   causal, self.zigzag, ring_mode == "chain", timeout_s)
+        # the per-call checks compare against these (built once: a call's host
+        # path is on the critical path of a step that starts from an idle GPU)
+        self._dev = torch.device("cuda", runtime.device)
+        self._shape_q = torch.Size((seq_per_rank, heads, head_dim))
+        self._shape_kv = torch.Size((seq_per_rank, self.heads_kv, head_dim))
+        self._default_scale = head_dim ** -0.5
 
     @property
     def rank(self) -> int:
@@ -74,18 +80,18 @@ class RingAttention:
         return self.runtime.world
 
     def _check_inputs(self, q, k, v, out=None):
-        exp_q = (self.seq, self.heads, self.head_dim)
-        exp_kv = (self.seq, self.heads_kv, self.head_dim)
-        dev = torch.device("cuda", self.runtime.device)
-        for name, t, shape in (("q", q, exp_q), ("k", k, exp_kv), ("v", v, exp_kv)):
-            if tuple(t.shape) != shape or t.dtype != self.dtype or t.device != dev:
-                raise ValueError(f"{name}: expected {self.dtype} tensor of shape {shape} on {dev}, "
+        dev, dt = self._dev, self.dtype
+        for name, t, shape in (("q", q, self._shape_q), ("k", k, self._shape_kv),
+                               ("v", v, self._shape_kv)):
+            if t.shape != shape or t.dtype != dt or t.device != dev:
+                raise ValueError(f"{name}: expected {dt} tensor of shape {tuple(shape)} on {dev}, "
                                  f"got {t.dtype} {tuple(t.shape)} on {t.device}")
-        if out is not None and (tuple(out.shape) != exp_q or out.device != dev
+        if out is not None and (out.shape != self._shape_q or out.device != dev
                                 or out.dtype not in (torch.float32, torch.bfloat16)
                                 or not out.is_contiguous()):
             raise ValueError(f"out: expected a contiguous float32/bfloat16 tensor of shape "
-                             f"{exp_q} on {dev}, got {out.dtype} {tuple(out.shape)} on {out.device}")
+                             f"{tuple(self._shape_q)} on {dev}, got {out.dtype} {tuple(out.shape)} "
+                             f"on {out.device}")
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  scale: Optional[float] = None, return_lse: bool = False,
@@ -97,7 +103,7 @@ class RingAttention:
         """
         self._check_inputs(q, k, v, out)
         if scale is None:
-            scale = self.head_dim ** -0.5
+            scale = self._default_scale
         if out is None:
             out = torch.empty_like(q)
         lse = (torch.empty(self.seq, self.heads, dtype=torch.float32, device=q.device)
