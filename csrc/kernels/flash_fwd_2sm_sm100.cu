@@ -692,6 +692,7 @@ int flash_forward_2sm_launch(const FlashParams& p, const CUtensorMap& tq, const 
   if (grid % 2 != 0 || grid <= 0) throw std::runtime_error("flash pair kernel: grid must be even");
   if (p.dynamic && !p.causal)
     throw std::runtime_error("flash pair kernel: dynamic claiming is for causal launches");
+  if (slot_stride == 0) slot_stride = ring_block_bytes(Prec::kBF16, p.Skv, p.Hkv, kD);
   // K in halves of 64 keys; V and Q in 128-row boxes of 64 columns
   uint64_t dims[4] = {(uint64_t)kD, (uint64_t)p.Hkv, (uint64_t)p.Skv, (uint64_t)p.nblk};
   uint64_t strides[3] = {(uint64_t)kD * 2, (uint64_t)p.Hkv * kD * 2, slot_stride};

@@ -2,6 +2,7 @@
 // replaces the reference's per-step ring loop (send/recv of the K/V shard, then
 // attention and merge of the current block; src/attention/
 // ring_attention_nccl_gpu_bench.cu:331-367) with one fused kernel launch per call.
+#include <cstdint>
 #include <stdexcept>
 
 #include "drivers.h"
@@ -119,6 +120,25 @@ void FusedRing::attend(const void* q, void* out, bool out_bf16, float* lse, floa
 
 void FusedRing::forward(const void* q, const void* k, const void* v, void* out, bool out_bf16,
                         float* lse, float scale, cudaStream_t stream) {
+  const bool aligned =
+      reinterpret_cast<uintptr_t>(k) % 16 == 0 && reinterpret_cast<uintptr_t>(v) % 16 == 0;
+  if (!args_.fused && args_.prec == Prec::kBF16 && aligned) {
+    // one rank, bf16: the ring slot would only be a copy of K/V in the same
+    // layout; the kernel reads the caller's K and V directly
+    TraceRange range("rab.fused_attention");
+    FlashArgs a = args_;
+    a.q = q;
+    a.k_base = k;
+    a.v_base = v;
+    a.slot_stride = 0;
+    a.out = out;
+    a.out_bf16 = out_bf16;
+    a.lse = lse;
+    a.scale = scale;
+    const int err = flash_run(a, plan_, stream);
+    cuda_check(static_cast<cudaError_t>(err), "ring attention launch");
+    return;
+  }
   prepare(k, v, stream);
   attend(q, out, out_bf16, lse, scale, stream);
 }
