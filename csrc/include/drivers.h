@@ -35,7 +35,8 @@ struct RingCopyParams {
   uint64_t base;            // steps completed by earlier launches
   DeviceStatus* status;
   uint64_t timeout_ns;
-  int mode;                 // 0: 16-byte vector stores, 1: TMA bulk copies through shared memory
+  int mode;                 // 0: 16-byte vector stores, 1: TMA bulk copies through shared
+                            // memory, 2: 32-byte vector loads and stores
 };
 int p2p_ring_launch(const RingCopyParams& p, int slices, cudaStream_t stream);
 
@@ -48,7 +49,7 @@ struct CommOptions {
   int warmup = 10;
   int iters = 100;
   int slices = 0;        // b200_fused CTAs (0: default)
-  int p2p_mode = 0;      // b200_fused copy engine: 0 vector stores, 1 TMA bulk
+  int p2p_mode = 0;      // b200_fused copy engine: 0 vector stores, 1 TMA bulk, 2 32-byte vectors
   bool precheck = true;
 };
 

@@ -57,11 +57,35 @@ __device__ bool wait_ge(const uint64_t* flag, uint64_t target, DeviceStatus* st,
 
 constexpr int kVecThreads = 512;
 constexpr int kVecUnroll = 4;                                   // chunks in flight per thread
-constexpr size_t kVecChunk16 = static_cast<size_t>(kVecThreads);  // 8 KiB chunks
+constexpr size_t kVecChunk16 = static_cast<size_t>(kVecThreads);  // one vector per thread
 
+// 16-byte (uint4) or 32-byte (sm_100 256-bit ld/st) vectors
+struct alignas(32) Vec32 {
+  uint32_t w[8];
+};
+
+__device__ __forceinline__ uint4 ld_vec(const uint4* p) { return __ldcg(p); }
+__device__ __forceinline__ void st_vec(uint4* p, const uint4& v) { *p = v; }
+__device__ __forceinline__ Vec32 ld_vec(const Vec32* p) {
+  Vec32 r;
+  asm volatile("ld.global.cg.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]), "=r"(r.w[4]),
+                 "=r"(r.w[5]), "=r"(r.w[6]), "=r"(r.w[7])
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_vec(Vec32* p, const Vec32& v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]),
+               "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]),
+               "r"(v.w[7])
+               : "memory");
+}
+
+// Chunks of kVecThreads vectors (8 KiB with 16-byte vectors, 16 KiB with 32-byte ones).
+template <typename V>
 __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyParams p) {
   const int c = blockIdx.x;
-  const size_t n16 = p.bytes / 16;
+  const size_t n16 = p.bytes / sizeof(V);
   const size_t stride16 = kVecChunk16 * gridDim.x;
   __shared__ int s_ok;
   for (int s = 0; s < p.nsteps; ++s) {
@@ -75,22 +99,22 @@ __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyPar
     }
     __syncthreads();
     if (!s_ok) return;
-    const uint4* src = reinterpret_cast<const uint4*>(p.buf[sg & 1]);
-    uint4* dst = reinterpret_cast<uint4*>(p.right_buf[(sg + 1) & 1]);
-    // chunks c, c + G, c + 2G, ... of 8 KiB (one 16-byte vector per thread),
-    // kVecUnroll of them in flight; the CTAs' shares differ by one chunk at most
+    const V* src = reinterpret_cast<const V*>(p.buf[sg & 1]);
+    V* dst = reinterpret_cast<V*>(p.right_buf[(sg + 1) & 1]);
+    // chunks c, c + G, c + 2G, ... (one vector per thread), kVecUnroll of them
+    // in flight; the CTAs' shares differ by one chunk at most
     size_t base = kVecChunk16 * c;
     for (; base + (kVecUnroll - 1) * stride16 + kVecChunk16 <= n16; base += kVecUnroll * stride16) {
       const size_t i = base + threadIdx.x;
-      uint4 r[kVecUnroll];
+      V r[kVecUnroll];
 #pragma unroll
-      for (int u = 0; u < kVecUnroll; ++u) r[u] = __ldcg(src + i + u * stride16);
+      for (int u = 0; u < kVecUnroll; ++u) r[u] = ld_vec(src + i + u * stride16);
 #pragma unroll
-      for (int u = 0; u < kVecUnroll; ++u) dst[i + u * stride16] = r[u];
+      for (int u = 0; u < kVecUnroll; ++u) st_vec(dst + i + u * stride16, r[u]);
     }
     for (; base < n16; base += stride16) {
       const size_t i = base + threadIdx.x;
-      if (i < n16) dst[i] = __ldcg(src + i);
+      if (i < n16) st_vec(dst + i, ld_vec(src + i));
     }
     // The barrier orders every thread's stores before thread 0's system-scope
     // release, and release is cumulative, so the neighbour that acquires
@@ -235,8 +259,10 @@ int p2p_ring_launch(const RingCopyParams& p, int slices, cudaStream_t stream) {
         p2p_ring_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
     p2p_ring_bulk_kernel<<<slices, 32, smem, stream>>>(p);
+  } else if (p.mode == 2 && p.bytes % 32 == 0) {
+    p2p_ring_kernel<Vec32><<<slices, kVecThreads, 0, stream>>>(p);
   } else {
-    p2p_ring_kernel<<<slices, kVecThreads, 0, stream>>>(p);
+    p2p_ring_kernel<uint4><<<slices, kVecThreads, 0, stream>>>(p);
   }
   return static_cast<int>(cudaGetLastError());
 }
