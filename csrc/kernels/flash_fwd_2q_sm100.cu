@@ -376,21 +376,16 @@ __global__ void __launch_bounds__(kThreads2, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], g & 1, st, kSiteSFull, tmo));
         if (!ok) break;
         tc_fence_after();
-        // The S row of this thread in two halves: the second half's TMEM load
-        // is issued once the first half has landed and runs while the first
-        // half is processed.
+        // the whole S row of this thread in registers
         uint32_t sr[kN];
-        tmem_ld32(s_col, sr);
-        tmem_ld32(s_col + 32, sr + 32);
-        tmem_ld_wait();
-        tmem_ld32(s_col + 64, sr + 64);
-        tmem_ld32(s_col + 96, sr + 96);
-        // only tiles the mask cuts (the same class for every row of the query
-        // tile, so the branch is uniform); full tiles skip the selects
-        const bool cut = kCausal && cls != 1;
-        if (cut) {
 #pragma unroll
-          for (int c = 0; c < kN / 2; ++c)
+        for (int c = 0; c < kN; c += 32) tmem_ld32(s_col + c, sr + c);
+        tmem_ld_wait();
+        if (kCausal && cls != 1) {
+          // only tiles the mask cuts (the same class for every row of the query
+          // tile, so the branch is uniform); full tiles skip the 128 selects
+#pragma unroll
+          for (int c = 0; c < kN; ++c)
             if (c > lim) sr[c] = 0xff800000u;  // -inf
         }
         // row max: 3-input max folds two new columns per instruction
@@ -398,48 +393,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sr[i]);
 #pragma unroll
-        for (int c = 8; c < kN / 2; c += 2)
-          pm[(c >> 1) & 7] =
-              fmax3(pm[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-        const float2 scale2 = make_float2(sl2, sl2);
-        // Exponentials, row sum and packed bf16 P of pairs [i0, i0 + 32) (P
-        // columns [i0, i0 + 32)); the scale-and-shift and the sums run as
-        // packed fp32 pairs.
-        auto exp_half = [&](int i0, float m_use) -> float {
-          const float2 shift2 = make_float2(-m_use, -m_use);
-          float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                           make_float2(0.f, 0.f)};
-          uint32_t pk[32];
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int i = i0 + jj;
-            const float2 xs = ffma2(make_float2(__uint_as_float(sr[2 * i]),
-                                                __uint_as_float(sr[2 * i + 1])),
-                                    scale2, shift2);
-            const float2 e = make_float2(ex2_approx(xs.x), ex2_approx(xs.y));
-            ps2[jj & 3] = fadd2(ps2[jj & 3], e);
-            pk[jj] = pack_bf16x2(e.x, e.y);
-          }
-          tmem_st32(s_col + i0, pk);
-          const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
-          return ps.x + ps.y;
-        };
-        // Speculation: after a unit's first tile the running max rarely moves
-        // (lazy rescale), so the first half's exponentials are formed with it
-        // while the second half loads, and redone if the row max moved.
-        const float mx1 = fmaxf(fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
-                                      pm[6]),
-                                pm[7]) * sl2;
-        const bool spec = __all_sync(0xffffffffu, j > 0 && mx1 <= m_run + kRescaleThreshold);
-        float l_first = spec ? exp_half(0, m_run == -INFINITY ? 0.f : m_run) : 0.f;
-        tmem_ld_wait();
-        if (cut) {
-#pragma unroll
-          for (int c = kN / 2; c < kN; ++c)
-            if (c > lim) sr[c] = 0xff800000u;
-        }
-#pragma unroll
-        for (int c = kN / 2; c < kN; c += 2)
+        for (int c = 8; c < kN; c += 2)
           pm[(c >> 1) & 7] =
               fmax3(pm[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
         const float mx = fmaxf(fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
@@ -452,8 +406,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           m_run = mx;
           l_run *= alpha;
         }
-        const bool any_need = __any_sync(0xffffffffu, need);
-        if (j > 0 && any_need) {
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
           // PV of this tile's previous step precedes this step's QK in the
           // MMA order, so it has completed; the wait is a safety net
           ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (g - 1) & 1, st, kSitePvDone, tmo));
@@ -470,9 +423,31 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        // lanes whose max did not move recompute the same values
-        if (!spec || any_need) l_first = exp_half(0, m_use);
-        l_run += l_first + exp_half(32, m_use);
+        // exponentials, row sum, packed bf16 P over the first 64 S columns;
+        // the scale-and-shift and the row sum run as packed fp32 pairs
+        const float2 scale2 = make_float2(sl2, sl2);
+        const float2 shift2 = make_float2(-m_use, -m_use);
+        float2 ps2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        // two halves of 32 packed columns: each half's P goes to TMEM before the
+        // next is formed (fewer live registers at the softmax's 216-register cap)
+#pragma unroll
+        for (int hlf = 0; hlf < 2; ++hlf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int i = hlf * 32 + j;
+            const float2 x = ffma2(make_float2(__uint_as_float(sr[2 * i]),
+                                               __uint_as_float(sr[2 * i + 1])),
+                                   scale2, shift2);
+            const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            ps2[j & 3] = fadd2(ps2[j & 3], e);
+            pk[j] = pack_bf16x2(e.x, e.y);
+          }
+          tmem_st32(s_col + hlf * 32, pk);
+        }
+        const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
+        l_run += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();  // the warp's TMEM stores are complete and fenced
