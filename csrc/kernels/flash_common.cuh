@@ -190,12 +190,15 @@ struct TileWalk {
   int k_lo;       // first global key position of tile v
   int t;          // tile within its block
   int chunk_end;  // tile (within the block) where the current chunk ends
-  int tpb, q_hi;
+  int q_hi;       // last global query position the walk serves
+  // (tiles per block, p.Skv / kN, is recomputed where needed: one register
+  // fewer in the softmax, which runs at its register cap)
 
   // position the walk at tile `v_new` (no visibility check)
   __device__ __forceinline__ void seek(const FlashParams& p, int v_new) {
     v = v_new;
     if (v >= v_end) return;
+    const int tpb = p.Skv / kN;
     const int s = v / tpb;
     t = v - s * tpb;
     const int tpc = p.zigzag ? tpb / 2 : tpb;
@@ -210,10 +213,8 @@ struct TileWalk {
     while (v < v_end && k_lo > q_hi) seek(p, v - t + chunk_end);
     return v < v_end;
   }
-  __device__ __forceinline__ bool begin(const FlashParams& p, int v_begin, int v_end_, int tpb_,
-                                        int q_hi_) {
+  __device__ __forceinline__ bool begin(const FlashParams& p, int v_begin, int v_end_, int q_hi_) {
     v_end = v_end_;
-    tpb = tpb_;
     q_hi = q_hi_;
     seek(p, v_begin);
     return settle(p);

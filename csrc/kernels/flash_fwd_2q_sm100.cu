@@ -55,6 +55,15 @@ constexpr uint32_t kRegsHigh = 216;    // softmax warpgroups
 static_assert(128 * kRegsLow + 256 * kRegsHigh <= kRegsLaunch * 384,
               "register split exceeds the launch allocation");
 
+// Causal launches: the MMA thread, which walks the visible KV tiles, hands the
+// softmax warps each tile's first global key position through a ring of
+// kKloSlots shared words (one mbarrier each; kKloEnd closes a work item), so
+// the softmax, at its register cap, carries no walk state of its own.  The
+// MMA thread is at most three entries ahead of either softmax warpgroup (it
+// waits for their P of the previous tiles), so the ring never laps a reader.
+constexpr int kKloSlots = 8;
+constexpr int kKloEnd = -2147483647 - 1;
+
 template <int D>
 struct Cfg2 {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
@@ -64,7 +73,7 @@ struct Cfg2 {
   static constexpr int kVTile = kKTile;
   static constexpr int kStages = D == 64 ? 4 : 2;
   static constexpr int kSmemTiles = 2 * kQTile + kStages * (kKTile + kVTile);
-  static constexpr int kNumBars = 4 * kStages + 10 + 2 * kItemSlots;
+  static constexpr int kNumBars = 4 * kStages + 10 + 2 * kItemSlots + kKloSlots;
   static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
   static constexpr int kKSteps = D / 16;   // QK: K = head dim, 16 bf16 per MMA
   static constexpr int kPSteps = kN / 16;  // PV: K = keys
@@ -114,9 +123,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t* drain = bars + 4 * NS + 9;
   uint64_t* item_full = bars + 4 * NS + 10;                 // [kItemSlots] work-item queue
   uint64_t* item_empty = bars + 4 * NS + 10 + kItemSlots;  // [kItemSlots]
+  uint64_t* klo_full = bars + 4 * NS + 10 + 2 * kItemSlots;  // [kKloSlots] (causal)
   __shared__ uint32_t tmem_slot;
   __shared__ int s_copy_ok;
   __shared__ Item s_items[kItemSlots];  // causal: TMA thread -> MMA and softmax roles
+  __shared__ int s_klo[kKloSlots];      // causal: MMA thread -> softmax, per visible tile
 
   const uint32_t warp = warp_id();
   DeviceStatus* st = p.status;
@@ -141,6 +152,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     for (int i = 0; i < kItemSlots; ++i) {
       mbar_init(&item_full[i], 1);
       mbar_init(&item_empty[i], 1 + 8);  // the MMA thread + one lane per softmax warp
+    }
+    for (int i = 0; i < kKloSlots; ++i) {
+      mbar_init(&klo_full[i], 1);
     }
     fence_barrier_init();
   }
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                         it.q0 + x * kM);
         TileWalk<kN> wk;
         int v = it.v_begin;
-        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                             : v < it.v_end;
         for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
           if constexpr (kCausal) v = wk.v;
@@ -248,6 +262,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     // ------------------------------------------------------------------ MMA
     if (elect_one()) {
       int g = 0, item_count = 0;
+      int e = 0;  // causal: entries written to the key-position ring
       bool ok = true;
       const uint32_t qbase = smem_u32(sQ);
       auto issue_qk = [&](int x, int stage) {
@@ -298,9 +313,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
         int j = 0;
         TileWalk<kN> wk;
         int v = it.v_begin;
-        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                             : v < it.v_end;
         for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+          if constexpr (kCausal) {
+            s_klo[e % kKloSlots] = wk.k_lo;
+            mbar_arrive(&klo_full[e % kKloSlots]);
+            ++e;
+          }
           const int stage = g % NS;
           ok = mbar_wait(&k_full[stage], (g / NS) & 1, st, kSiteKFull, tmo);
           if (!ok) break;
@@ -316,6 +336,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!ok) break;
           ++j;
           ++g;
+        }
+        if (kCausal && ok) {  // the softmax's end of this item
+          s_klo[e % kKloSlots] = kKloEnd;
+          mbar_arrive(&klo_full[e % kKloSlots]);
+          ++e;
         }
         if (ok && j > 0) {
           ok = issue_pv(1, g - 1, j == 1);
@@ -339,6 +364,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const uint32_t s_col = tmem + lane_base + col_s(x);
     const uint32_t o_col = tmem + lane_base + col_o(x);
     int g = 0, final_count = 0;
+    int e = 0;  // causal: entries read from the key-position ring
     bool ok = true;
     for (int w = 0; ok; ++w) {
       const int slot = w % kItemSlots;
@@ -355,21 +381,28 @@ __global__ void __launch_bounds__(kThreads2, 1)
         it = make_item(p, item, tiles_total);
       }
       const int q0 = it.q0 + x * kM;
-      const int qrow = q0 + row;
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       // global positions of this warpgroup's query tile (causal classification)
       const int q_lo_own = kCausal ? global_pos(q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
-      TileWalk<kN> wk;
-      int v = it.v_begin;
-      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
-                          : v < it.v_end;
-      for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
+      int v = it.v_begin;  // non-causal: the tile
+      int k_lo = 0;        // causal: the tile's first global key position (MMA thread)
+      // causal: the next visible tile of this item from the ring; false at its end
+      auto next_klo = [&]() -> bool {
+        const int ks = e % kKloSlots;
+        ok = __all_sync(0xffffffffu, mbar_wait(&klo_full[ks], (e / kKloSlots) & 1, st,
+                                               kSiteSFull, tmo));
+        if (!ok) return false;
+        k_lo = s_klo[ks];
+        ++e;
+        return k_lo != kKloEnd;
+      };
+      bool more = kCausal ? next_klo() : v < it.v_end;
+      for (; more && ok; more = kCausal ? next_klo() : ++v < it.v_end) {
         int lim = kN;   // visible columns: c <= lim
         int cls = 1;    // this query tile's class of the tile: 0 masked, 1 full, 2 diagonal
         if constexpr (kCausal) {
           // the tile is visible to the unit; classify it for this query tile
-          const int k_lo = wk.k_lo;
           cls = k_lo > q_lo_own + kM - 1 ? 0 : (k_lo + kN - 1 <= q_lo_own ? 1 : 2);
           lim = cls == 0 ? -1 : (cls == 2 ? q_lo_own + row - k_lo : kN);
         }
@@ -465,15 +498,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tc_fence_after();
       }
       const float m_nat = have ? m_run * kLn2 : -INFINITY;
-      const size_t r = static_cast<size_t>(qrow) * p.Hq + it.h;
-      const bool split = it.store >= 0;
+      // the item again (queue slot or static list) rather than kept live across
+      // the tile loop: the causal softmax runs at its register cap
+      const Item ie = kCausal ? s_items[slot] : make_item(p, blockIdx.x + w * gridDim.x,
+                                                         tiles_total);
+      const int qrow = ie.q0 + x * kM + row;
+      const size_t r = static_cast<size_t>(qrow) * p.Hq + ie.h;
+      const bool split = ie.store >= 0;
       // (RAB_DEBUG_BOUNDS builds: an out-of-range row or record is reported, its stores skipped)
       const bool out_in =
-          st_bounds(st, qrow < p.Sq && it.h < p.Hq && (!split || it.store < p.n_items),
-                    split ? kBoundsRecord : kBoundsQRow, split ? it.store : qrow);
+          st_bounds(st, qrow < p.Sq && ie.h < p.Hq && (!split || ie.store < p.n_items),
+                    split ? kBoundsRecord : kBoundsQRow, split ? ie.store : qrow);
       const float inv = (have && l_run > 0.f && !p.partial && !split) ? 1.f / l_run : 1.f;
       const size_t srow =
-          static_cast<size_t>(split ? it.store : 0) * p.rows_per_unit + x * kM + row;
+          static_cast<size_t>(split ? ie.store : 0) * p.rows_per_unit + x * kM + row;
       float* dst_f32 = nullptr;
       if (split)
         dst_f32 = p.split_acc + srow * D;

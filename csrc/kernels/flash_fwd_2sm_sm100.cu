@@ -245,7 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
                           it.q0 + x * 256 + static_cast<int>(crank) * kM);
           TileWalk<kN> wk;
           int v = it.v_begin;
-          bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+          bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                               : v < it.v_end;
           for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
             if constexpr (kCausal) v = wk.v;
@@ -342,7 +342,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             int j = 0;
             TileWalk<kN> wk;
             int v = it.v_begin;
-            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                                 : v < it.v_end;
             for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
               const int stage = g % kStages;
@@ -394,7 +394,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
             mbar_arrive_cluster(leader_bar(q_full));
             TileWalk<kN> wk;
             int v = it.v_begin;
-            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+            bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                                 : v < it.v_end;
             for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
               const int stage = g % kStages;
@@ -445,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
       const int q_lo_own = kCausal ? global_pos(q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
       TileWalk<kN> wk;
       int v = it.v_begin;
-      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, unit_q_hi(p, it.q0))
+      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, unit_q_hi(p, it.q0))
                           : v < it.v_end;
       for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
         int lim = kN;

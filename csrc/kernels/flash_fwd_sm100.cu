@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         TileWalk<kN> wk;
         int v = it.v_begin;
-        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, tile_q_hi(p, it.q0))
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tile_q_hi(p, it.q0))
                             : v < it.v_end;
         for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
           if constexpr (kCausal) v = wk.v;
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         TileWalk<kN> wk;
         int v = it.v_begin;
-        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, tile_q_hi(p, it.q0))
+        bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tile_q_hi(p, it.q0))
                             : v < it.v_end;
         for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
           const int stage = g % NS;
@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q_lo = kCausal ? global_pos(it.q0, p.rank, p.Sq, p.world, p.zigzag) : 0;
       TileWalk<kN> wk;
       int v = it.v_begin;
-      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, tpb, q_lo + kM - 1)
+      bool more = kCausal ? wk.begin(p, it.v_begin, it.v_end, q_lo + kM - 1)
                           : v < it.v_end;
       for (; more && ok; more = kCausal ? wk.next(p) : ++v < it.v_end) {
         int k_lo = 0;
@@ -755,46 +755,82 @@ __global__ void split_merge_kernel(const FlashParams p) {
   write_merged<D>(p, unit, row, c, mx, l, a);
 }
 
-// Balanced schedule: blockIdx.y + 1 = b indexes the boundary between CTAs b-1
-// and b in the shared-out remainder.  A boundary strictly inside unit u, and
-// the first such boundary of u, merges u from the records of CTAs b-1, b, ...
-// whose ranges meet u (record 2c when u holds the first tile of CTA c's
-// range, else 2c + 1).
+// Balanced schedule: blockIdx.x = unit - full_waves * G over the units of the
+// shared-out remainder, blockIdx.y = the block's kBalMergeRows rows of it.  CTA c of G owns the tiles
+// [c*T/G, (c+1)*T/G), so the CTAs whose ranges meet the unit's tiles
+// [u0, u1) are c_lo = owner(u0) .. c_hi = owner(u1 - 1), owner(x) =
+// floor(((x + 1) G - 1) / T) (the last CTA whose range starts at or before
+// x).  A unit inside one CTA's range was written whole by that CTA; otherwise
+// the pieces are merged from record 2c (the unit holds the first tile of CTA
+// c's range) or 2c + 1 (it holds its last) of each of those CTAs.
+constexpr int kBalMergeRows = 16;  // rows of a unit per block (blockIdx.y picks them)
+constexpr int kBalMaxPieces = 16;
+
 template <int D>
 __global__ void balanced_merge_kernel(const FlashParams p) {
   constexpr int kTpr = D / 4;
   const int G = p.n_items;
-  const int b = blockIdx.y + 1;
   const long long tt = p.kv_tiles;
   const int base = p.full_waves * G;
   const long long T = static_cast<long long>(p.n_units - base) * tt;
-  const long long bt = balanced_start(T, G, b);
-  const int urel = static_cast<int>(bt / tt);
-  const long long u0 = urel * tt;
-  const int unit = base + urel;
-  if (bt == u0 || balanced_start(T, G, b - 1) > u0) return;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  const int row = t / kTpr;
-  const int c = t % kTpr;
-  if (row >= kM) return;
-  float mx = -INFINITY;
-  for (int cta = b - 1; cta < G; ++cta) {
-    const long long s = balanced_start(T, G, cta);
-    if (s >= u0 + tt) break;
-    if (balanced_start(T, G, cta + 1) <= s) continue;  // empty range
-    const size_t rec = 2 * static_cast<size_t>(cta) + (s >= u0 ? 0 : 1);
-    mx = fmaxf(mx, p.split_m[rec * kM + row]);
+  const long long u0 = static_cast<long long>(blockIdx.x) * tt;
+  const long long u1 = u0 + tt;
+  const int c_lo = static_cast<int>(((u0 + 1) * G - 1) / T);
+  const int c_hi = static_cast<int>((u1 * G - 1) / T);
+  if (c_lo >= c_hi) return;  // written whole by one CTA
+  const int unit = base + static_cast<int>(blockIdx.x);
+  // record of the k-th CTA's piece of the unit (-1: empty range)
+  auto record = [&](int c) -> long long {
+    const long long s_c = balanced_start(T, G, c);
+    if (balanced_start(T, G, c + 1) <= s_c) return -1;
+    return 2LL * c + (s_c >= u0 ? 0 : 1);
+  };
+  if (c_hi - c_lo + 1 <= kBalMaxPieces) {
+    // the usual case (a unit spans about tt * G / T + 1 CTAs): the records
+    // once per block, not inside the row loops
+    __shared__ size_t rec[kBalMaxPieces];
+    __shared__ int s_n;
+    if (threadIdx.x == 0) {
+      int k = 0;
+      for (int c = c_lo; c <= c_hi; ++c) {
+        const long long r = record(c);
+        if (r >= 0) rec[k++] = static_cast<size_t>(r);
+      }
+      s_n = k;
+    }
+    __syncthreads();
+    const int n = s_n;
+    for (int q = threadIdx.x; q < kBalMergeRows * kTpr; q += blockDim.x) {
+      const int row = blockIdx.y * kBalMergeRows + q / kTpr;
+      const int c = q % kTpr;
+      float mx = -INFINITY;
+      for (int i = 0; i < n; ++i) mx = fmaxf(mx, p.split_m[rec[i] * kM + row]);
+      const float mref = (mx == -INFINITY) ? 0.f : mx;
+      float l = 0.f;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = 0; i < n; ++i) add_record<D>(p, rec[i], kM, row, c, mref, l, a);
+      write_merged<D>(p, unit, row, c, mx, l, a);
+    }
+    return;
   }
-  const float mref = (mx == -INFINITY) ? 0.f : mx;
-  float l = 0.f;
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int cta = b - 1; cta < G; ++cta) {
-    const long long s = balanced_start(T, G, cta);
-    if (s >= u0 + tt) break;
-    if (balanced_start(T, G, cta + 1) <= s) continue;
-    add_record<D>(p, 2 * static_cast<size_t>(cta) + (s >= u0 ? 0 : 1), kM, row, c, mref, l, a);
+  // a unit cut by many CTAs (few units left over for many CTAs)
+  for (int q = threadIdx.x; q < kBalMergeRows * kTpr; q += blockDim.x) {
+    const int row = blockIdx.y * kBalMergeRows + q / kTpr;
+    const int c = q % kTpr;
+    float mx = -INFINITY;
+    for (int k = c_lo; k <= c_hi; ++k) {
+      const long long r = record(k);
+      if (r >= 0) mx = fmaxf(mx, p.split_m[static_cast<size_t>(r) * kM + row]);
+    }
+    const float mref = (mx == -INFINITY) ? 0.f : mx;
+    float l = 0.f;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = c_lo; k <= c_hi; ++k) {
+      const long long r = record(k);
+      if (r >= 0) add_record<D>(p, static_cast<size_t>(r), kM, row, c, mref, l, a);
+    }
+    write_merged<D>(p, unit, row, c, mx, l, a);
   }
-  write_merged<D>(p, unit, row, c, mx, l, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -1009,13 +1045,14 @@ int flash_forward_launch(Prec prec, const FlashParams& p, const FlashMaps& maps,
 
 int flash_split_merge_launch(const FlashParams& p, cudaStream_t stream) {
   if (p.balanced) {
-    if (p.n_items < 2) return 0;
-    const int bs = 256;
-    const dim3 grid((kM * (p.D / 4) + bs - 1) / bs, p.n_items - 1);
+    const int remainder = p.n_units - p.full_waves * p.n_items;  // units shared out
+    if (p.n_items < 2 || remainder <= 0) return 0;
+    const dim3 grid(remainder, kM / kBalMergeRows);
+    const int threads = kBalMergeRows * (p.D / 4);  // one float4 of one row each
     if (p.D == 64)
-      balanced_merge_kernel<64><<<grid, bs, 0, stream>>>(p);
+      balanced_merge_kernel<64><<<grid, threads, 0, stream>>>(p);
     else
-      balanced_merge_kernel<128><<<grid, bs, 0, stream>>>(p);
+      balanced_merge_kernel<128><<<grid, threads, 0, stream>>>(p);
     return static_cast<int>(cudaGetLastError());
   }
   const long long threads_total = static_cast<long long>(p.n_units) * p.rows_per_unit * (p.D / 4);
