@@ -81,6 +81,7 @@ def test_ring_blocks_gqa(cuda_device, dtype, d, nsplit):
     (torch.bfloat16, 128, 4096, 8, 1),   # 256 query tiles: whole tiles plus cut ones per CTA
     (torch.bfloat16, 64, 384, 3, 2),     # fewer (tile, KV tile) pairs than CTAs: empty ranges
     (torch.bfloat16, 64, 512, 37, 1),    # 148 query tiles: one whole wave on a 148-SM B200
+    (torch.float32, 64, 128, 1, 9),      # one query tile cut into 18 one-tile pieces (> 16)
 ])
 def test_balanced_schedule(cuda_device, dtype, d, spr, heads, world):
     """Balanced schedule (nsplit=-1): whole waves of query tiles, then equal
