@@ -30,6 +30,9 @@ def check_line(d, n_gpus, steps, warmup):
     assert E2E_KEYS <= d["e2e"].keys() and d["e2e"]["value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] > 0 and d["e2e"]["d2h_bytes_per_step"] > 0
     assert isinstance(d["gpu_launches"], int) and d["gpu_launches"] >= steps
+    # the output check against the float64 recomputation ran and passed
+    chk = d["config"]["check"]
+    assert chk["passed"] is True and chk["max_abs_err"] <= chk["tol"], chk
 
 
 def _run(*args, env=None):
