@@ -369,7 +369,7 @@ def main() -> int:
 
     nsplit = attn.engine.nsplit
     # ring-format prep (fp32, one launch), the fused kernel, the merge pass (split or balanced)
-    per_step = (1 if dt == "fp32" else 0) + 1 + (1 if nsplit != 1 else 0)
+    per_step = (1 if dt == "fp32" else 0) + 1 + attn.engine.merge_launches
     if rank == 0:
         line = {
             "metric": METRIC,

@@ -271,6 +271,7 @@ void register_flash(pybind11::module_& m) {
         d["n_items"] = pl.n_items;
         d["grid"] = pl.grid;
         d["workspace_bytes"] = pl.workspace_bytes;
+        d["merge_kernel"] = pl.merge_kernel;
         return d;
       },
       pybind11::arg("prec"), pybind11::arg("Sq"), pybind11::arg("Skv"), pybind11::arg("nblk"),

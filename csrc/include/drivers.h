@@ -98,6 +98,7 @@ class FusedRing {
   uint8_t* slot0_v() const;
   int grid() const { return plan_.grid; }
   int nsplit() const { return plan_.balanced ? -1 : plan_.nsplit; }  // -1: balanced schedule
+  int merge_launches() const { return plan_.merge_kernel; }  // merge launches per call
   const FlashArgs& args() const { return args_; }  // shapes and precision of the engine
   uint64_t launches() const { return epoch_; }
   // Overlap trace of the following launches (FlashParams::stamps), one

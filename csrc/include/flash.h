@@ -195,6 +195,7 @@ struct FlashPlan {
   int n_units;
   int n_items;
   int grid;
+  int merge_kernel;   // 1: a merge launch follows the attention kernel (split records)
   size_t workspace_bytes;
 };
 

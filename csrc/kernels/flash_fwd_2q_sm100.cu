@@ -8,7 +8,9 @@
 // behind little tensor work, and the tensor pipe idles half the time.  Here
 // the tensor core alternates between two independent tiles A and B,
 //     QK_A(j), PV_B(j-1), QK_B(j), PV_A(j), QK_A(j+1), ...
-// so each tile's softmax runs while the other tile's GEMMs execute.
+// so each tile's softmax runs while the other tile's GEMMs execute.  Causal
+// launches hand P over in two 64-key halves, so PV starts half a softmax
+// earlier.
 //
 // CTA = 12 warps, persistent over work items (head, 256-row query unit, KV chunk):
 //   warp 0      TMA producer: Q_A / Q_B once per item, K / V tiles per step
@@ -28,6 +30,8 @@
 
 #include <cfloat>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 
@@ -73,7 +77,7 @@ struct Cfg2 {
   static constexpr int kVTile = kKTile;
   static constexpr int kStages = D == 64 ? 4 : 2;
   static constexpr int kSmemTiles = 2 * kQTile + kStages * (kKTile + kVTile);
-  static constexpr int kNumBars = 4 * kStages + 10 + 2 * kItemSlots + kKloSlots;
+  static constexpr int kNumBars = 4 * kStages + 10 + 2 * kItemSlots + kKloSlots + 2;
   static constexpr int kSmemBytes = kSmemTiles + 1024 + kNumBars * 8 + 64;
   static constexpr int kKSteps = D / 16;   // QK: K = head dim, 16 bf16 per MMA
   static constexpr int kPSteps = kN / 16;  // PV: K = keys
@@ -93,8 +97,10 @@ __device__ __forceinline__ int unit_q_hi(const FlashParams& p, int q0) {
 }
 
 // kCausal: tiles are classified against the causal mask; a non-causal
-// instantiation treats every tile as full.
-template <int D, bool kCausal>
+// instantiation treats every tile as full.  kPParts = 2: the softmax hands P
+// over in two halves of 64 keys (p_full, then p_hi), so the PV MMAs of the
+// first half start while the second half's exponentials are computed.
+template <int D, bool kCausal, int kPParts>
 __global__ void __launch_bounds__(kThreads2, 1)
     flash_fwd_2q_kernel(const __grid_constant__ FlashParams p,
                         const __grid_constant__ CUtensorMap tmQ,
@@ -124,6 +130,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint64_t* item_full = bars + 4 * NS + 10;                 // [kItemSlots] work-item queue
   uint64_t* item_empty = bars + 4 * NS + 10 + kItemSlots;  // [kItemSlots]
   uint64_t* klo_full = bars + 4 * NS + 10 + 2 * kItemSlots;  // [kKloSlots] (causal)
+  uint64_t* p_hi = klo_full + kKloSlots;                      // [2] (kPParts == 2)
   __shared__ uint32_t tmem_slot;
   __shared__ int s_copy_ok;
   __shared__ Item s_items[kItemSlots];  // causal: TMA thread -> MMA and softmax roles
@@ -145,6 +152,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 4);  // one arrival per softmax warp
+      mbar_init(&p_hi[x], 4);
       mbar_init(&pv_done[x], 1);
     }
     mbar_init(o_final, 1);
@@ -285,6 +293,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const uint32_t vb = smem_u32(sV + stage * C::kVTile);
 #pragma unroll
         for (int ks = 0; ks < C::kPSteps; ++ks) {
+          if (kPParts == 2 && ks == C::kPSteps / 2) {  // keys 64..127 of P
+            if (!mbar_wait(&p_hi[x], gp & 1, st, kSitePFull, tmo)) return false;
+            tc_fence_after();
+          }
           const uint64_t bdesc = make_sdesc(vb + ks * 2048, kN * 128, 1024);
           mma_ts<false>(tmem + col_o(x), tmem + col_s(x) + ks * 8, bdesc, C::kIdescPV,
                         (first && ks == 0) ? 0u : 1u);
@@ -478,13 +490,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
             pk[j] = pack_bf16x2(e.x, e.y);
           }
           tmem_st32(s_col + hlf * 32, pk);
+          if (kPParts == 2 && hlf == 0) {  // keys 0..63 of P are ready for the MMA
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane_id() == 0) mbar_arrive(&p_full[x]);
+          }
         }
         const float2 ps = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
         l_run += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();  // the warp's TMEM stores are complete and fenced
-        if (lane_id() == 0) mbar_arrive(&p_full[x]);
+        if (lane_id() == 0) mbar_arrive(kPParts == 2 ? &p_hi[x] : &p_full[x]);
         ++j;
         ++g;
       }
@@ -588,7 +606,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   }
 }
 
-template <int D, bool kCausal>
+template <int D, bool kCausal, int kPParts>
 int launch2(const FlashParams& p, const CUtensorMap& tq, const FlashMaps& maps, int grid,
             bool cooperative, cudaStream_t stream) {
   using C = Cfg2<D>;
@@ -596,7 +614,7 @@ int launch2(const FlashParams& p, const CUtensorMap& tq, const FlashMaps& maps, 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    cudaFuncSetAttribute(flash_fwd_2q_kernel<D, kCausal>,
+    cudaFuncSetAttribute(flash_fwd_2q_kernel<D, kCausal, kPParts>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
@@ -604,10 +622,10 @@ int launch2(const FlashParams& p, const CUtensorMap& tq, const FlashMaps& maps, 
     void* args[] = {const_cast<FlashParams*>(&p), const_cast<CUtensorMap*>(&tq),
                     const_cast<CUtensorMap*>(&maps.k), const_cast<CUtensorMap*>(&maps.v)};
     return static_cast<int>(cudaLaunchCooperativeKernel(
-        reinterpret_cast<void*>(flash_fwd_2q_kernel<D, kCausal>), dim3(grid), dim3(kThreads2), args,
+        reinterpret_cast<void*>(flash_fwd_2q_kernel<D, kCausal, kPParts>), dim3(grid), dim3(kThreads2), args,
         C::kSmemBytes, stream));
   }
-  flash_fwd_2q_kernel<D, kCausal><<<grid, kThreads2, C::kSmemBytes, stream>>>(p, tq, maps.k, maps.v);
+  flash_fwd_2q_kernel<D, kCausal, kPParts><<<grid, kThreads2, C::kSmemBytes, stream>>>(p, tq, maps.k, maps.v);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -626,11 +644,22 @@ int flash_forward_2q_launch(const FlashParams& p, const CUtensorMap& tq, const F
     throw std::runtime_error("flash 2q: needs 256-row units");
   if (p.Skv % 128 != 0) throw std::runtime_error("flash 2q: keys per block must be a multiple of 128");
   if (p.D == 64)
-    return p.causal ? launch2<64, true>(p, tq, maps, grid, cooperative, stream)
-                    : launch2<64, false>(p, tq, maps, grid, cooperative, stream);
-  if (p.D == 128)
-    return p.causal ? launch2<128, true>(p, tq, maps, grid, cooperative, stream)
-                    : launch2<128, false>(p, tq, maps, grid, cooperative, stream);
+    return p.causal ? launch2<64, true, 1>(p, tq, maps, grid, cooperative, stream)
+                    : launch2<64, false, 1>(p, tq, maps, grid, cooperative, stream);
+  if (p.D == 128) {
+    // P in two halves for causal launches (measured on B200, 16k x 32 heads:
+    // 1160 vs 1029 TFLOP/s; 64k GQA: 1164 vs 1075), whole for non-causal ones
+    // (1139 vs 1247); RAB_FLASH_PSPLIT=1|2 overrides for comparison
+    const char* e = std::getenv("RAB_FLASH_PSPLIT");
+    const bool two = e != nullptr && (std::strcmp(e, "1") == 0 || std::strcmp(e, "2") == 0)
+                         ? std::strcmp(e, "2") == 0
+                         : p.causal != 0;
+    if (two)
+      return p.causal ? launch2<128, true, 2>(p, tq, maps, grid, cooperative, stream)
+                      : launch2<128, false, 2>(p, tq, maps, grid, cooperative, stream);
+    return p.causal ? launch2<128, true, 1>(p, tq, maps, grid, cooperative, stream)
+                    : launch2<128, false, 1>(p, tq, maps, grid, cooperative, stream);
+  }
   throw std::runtime_error("flash 2q: head_dim must be 64 or 128");
 }
 

@@ -34,9 +34,6 @@ const FlashMaps& cached_maps(Prec prec, const void* k, const void* v, size_t str
   return cache.emplace(key, flash_make_maps(prec, k, v, stride, nblk, Skv, Hkv, D)).first->second;
 }
 
-// The two-query-tile bf16 kernel is opt-in (RAB_FLASH_2Q=1): measured on B200
-// it trails the one-tile kernel, whose head-major work order already keeps
-// the tensor and exp pipes equally busy.
 // Dynamic claiming of work items (causal one-tile launches) is on unless
 // RAB_FLASH_DYNAMIC=0.
 bool dynamic_enabled() {
@@ -190,6 +187,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
     pl.grid = a.grid > 0 ? a.grid : sms;
     pl.n_items = pl.grid;  // one balanced range per CTA
     pl.full_waves = pl.n_units / pl.grid;
+    pl.merge_kernel = 1;
     pl.workspace_bytes = static_cast<size_t>(2 * pl.grid) * 128 * (a.D + 2) * sizeof(float);
     return pl;
   }
@@ -206,6 +204,7 @@ FlashPlan flash_plan(const FlashArgs& a) {
   pl.grid = a.grid > 0 ? a.grid : std::min(pl.n_items, sms);
   if (a.fused) pl.grid = a.grid > 0 ? a.grid : sms;  // every CTA also copies a slice
   if (pair) pl.grid = 2 * (a.fused ? sms : std::min(pl.n_items, sms));  // two CTAs per worker
+  pl.merge_kernel = pl.nsplit > 1 ? 1 : 0;
   pl.workspace_bytes = pl.nsplit > 1 ? static_cast<size_t>(pl.n_items) * pl.rows_per_unit *
                                            (a.D + 2) * sizeof(float)
                                      : 0;
@@ -287,7 +286,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
     err = flash_forward_launch(a.prec, p, maps, pl.grid, a.fused, stream);
   }
   if (err != 0) return err;
-  if (records) err = flash_split_merge_launch(p, stream);
+  if (records && pl.merge_kernel) err = flash_split_merge_launch(p, stream);
   return err;
 }
 

@@ -284,6 +284,7 @@ void register_runtime(py::module_& m) {
            })
       .def_property_readonly("grid", &FusedRing::grid)
       .def_property_readonly("nsplit", &FusedRing::nsplit)
+      .def_property_readonly("merge_launches", &FusedRing::merge_launches)
       .def_property_readonly("launches", &FusedRing::launches)
       .def("slot0_ptrs", [](FusedRing& f) {
         return std::make_pair(reinterpret_cast<uintptr_t>(f.slot0_k()),
