@@ -45,6 +45,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "ring_attention_fwd_tflops"
+HOLD_CYCLES = 1_000_000  # device-side hold before each timed step: ~0.5 ms at 1965 MHz
 # name: (tokens per rank, q heads, kv heads, head dim, dtype, causal, input scale, seed)
 PRESETS = {
     # the reference's full ring attention at its largest ATTENTION_SIZES entry
@@ -253,11 +254,14 @@ def main() -> int:
     for i in range(args.steps):
         torch.cuda.synchronize(dev)
         rt.barrier()
-        # The L2 flush (a 256 MiB write) is enqueued right before the start
-        # event on the same stream: it runs between the steps, and while the
-        # GPU writes it the host enqueues the step, so the events bracket the
-        # device's work for the step and not the host's launch latency (the e2e
-        # figure below keeps every host cost).
+        # A fixed ~0.5 ms device-side delay (torch's cycle-count spin kernel)
+        # and the L2 flush (a 256 MiB write) are enqueued right before the
+        # start event on the same stream: they run between the steps, and
+        # while the GPU works on them the host enqueues the step, so the events
+        # bracket the device's work for the step, not the host's launch latency
+        # (which, with eight rank processes launching at once, also skews the
+        # ranks' start times; the e2e figure below keeps every host cost).
+        torch.cuda._sleep(HOLD_CYCLES)
         flush.fill_(i & 0xFF)
         starts[i].record(stream)
         attn(q, k, v, out=out)
@@ -401,6 +405,8 @@ def main() -> int:
                 "overlap": overlap,
                 "l2": "256 MiB buffer written before every timed step, enqueued on the same "
                       "stream just ahead of the start event (outside the events)",
+                "step_start": "after a host barrier, a ~0.5 ms device-side hold and the L2 "
+                              "flush, so the events time device work, not host launch latency",
                 "host_affinity": host_affinity,
                 "flops_per_step_total": flops_total,
                 "wall_ms_bracketed_loop": round(wall_ms, 3),

@@ -97,18 +97,42 @@ std::vector<std::pair<int, int>> visible_ranges(const FlashArgs& a, int kN, int 
   return r;
 }
 
-// nsplit for a causal launch with dynamic claiming: simulate the CTAs claiming
-// items in kernel order (chunk-major, then head-major units with the last
-// query tiles first) and keep the split with the shortest makespan.  A unit of
-// `rows` query rows works on every KV tile visible to its last 128-row tile,
-// once per 128-row tile; an item costs that work plus `overhead`, and a split
-// adds one merge pass.
-int causal_split(const FlashArgs& a, int kN, int rows, int units, int tiles, int sms,
-                 int overhead) {
+// Fused ring launches: the copy warps pull the other ranks' blocks in ring
+// order, block s landing about s copy intervals after the launch.  Measured on
+// B200 with 8 ranks: 268 MB bf16 blocks every 0.9 ms (~300 GB/s per GPU while
+// the tensor cores run).  The tile time converts that interval into the
+// planner's unit, one 128-row x kN-key tile on one SM, at the kernels'
+// measured rates (two-tile bf16 ~1.1 PFLOP/s, 3xTF32 ~0.24 PFLOP/s per GPU).
+constexpr double kRingCopyBytesPerS = 300e9;
+constexpr double kHbmBytesPerS = 6.5e12;
+
+double tile_seconds(const FlashArgs& a, int kN, int sms) {
+  const double rate = a.prec == Prec::kF32x3 ? 0.24e15 : 1.1e15;
+  return 4.0 * 128 * kN * a.D / (rate / sms);
+}
+
+// nsplit by simulation, for a causal launch with dynamic claiming and for any
+// fused ring launch of several blocks: simulate the CTAs claiming items in
+// kernel order (chunk-major, then head-major units, under a causal mask with
+// the last query tiles first) and keep the split with the shortest makespan.
+// A unit of `rows` query rows works on every KV tile visible to its last
+// 128-row tile (every tile without a mask), once per 128-row tile; an item
+// costs that work plus `overhead`, and a split adds one merge pass.  (The
+// non-causal static order hands equal items round-robin, which the claim
+// simulation reproduces.)  In a fused ring launch an item walks its chunk's ring
+// blocks in order and cannot start on block s before the block has landed, so
+// every CTA would wait for each block in turn when all items span the whole
+// ring; a split whose chunks follow the blocks lets the early items run on the
+// blocks already present.  There the merge pass is charged by its traffic
+// (every split's partial records read once).
+int simulated_split(const FlashArgs& a, int kN, int rows, int units, int tiles, int sms,
+                    int overhead) {
   static std::mutex mu;
   static std::map<std::vector<long long>, int> cache;
-  const std::vector<long long> key{a.Sq, a.Skv,   a.nblk, a.Hq,  a.world,  a.rank,
-                                   a.blk_offset, a.zigzag, kN, rows, sms, overhead};
+  const std::vector<long long> key{a.Sq,     a.Skv,    a.nblk, a.Hq,  a.Hkv, a.D,
+                                   a.world,  a.rank,   a.blk_offset, a.zigzag, a.fused ? 1 : 0,
+                                   a.causal,
+                                   static_cast<long long>(a.prec), kN, rows, sms, overhead};
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
@@ -117,7 +141,23 @@ int causal_split(const FlashArgs& a, int kN, int rows, int units, int tiles, int
   const int per_head = a.Sq / rows;
   const int weight = rows / 128;
   std::vector<std::vector<std::pair<int, int>>> vis(per_head);
-  for (int qt = 0; qt < per_head; ++qt) vis[qt] = visible_ranges(a, kN, qt * rows + rows - 128);
+  const int tpb = tiles / std::max(1, a.nblk);
+  for (int qt = 0; qt < per_head; ++qt) {
+    if (a.causal) {
+      vis[qt] = visible_ranges(a, kN, qt * rows + rows - 128);
+    } else {
+      for (int s = 0; s < a.nblk; ++s) vis[qt].emplace_back(s * tpb, (s + 1) * tpb);
+    }
+  }
+  // fused ring: arrival of block s, and the merge pass per split, in tile units
+  const bool ring = a.fused && a.nblk > 1;
+  double interval = 0.0, merge_per_split = 0.0;
+  if (ring) {
+    const double tile_s = tile_seconds(a, kN, sms);
+    interval = static_cast<double>(ring_block_bytes(a.prec, a.Skv, a.Hkv, a.D)) /
+               kRingCopyBytesPerS / tile_s;
+    merge_per_split = static_cast<double>(a.Sq) * a.Hq * (a.D + 2) * 4 / kHbmBytesPerS / tile_s;
+  }
   int best = 1;
   double best_span = 1e300;
   for (int ns = 1; ns <= 16 && ns <= tiles; ++ns) {
@@ -131,15 +171,20 @@ int causal_split(const FlashArgs& a, int kN, int rows, int units, int tiles, int
       const int ve = static_cast<int>(static_cast<long long>(c + 1) * tiles / ns);
       for (int u = 0; u < units; ++u) {
         const int qt = per_head - 1 - u % per_head;  // the kernel's unit order
-        int n = 0;
-        for (const auto& r : vis[qt]) n += std::max(0, std::min(r.second, ve) - std::max(r.first, vb));
-        const double t = load.top() + static_cast<double>(weight) * n + overhead;
+        double t = load.top();
+        for (const auto& r : vis[qt]) {  // ranges lie inside one ring block, in ring order
+          const int n = std::max(0, std::min(r.second, ve) - std::max(r.first, vb));
+          if (n == 0) continue;
+          if (ring) t = std::max(t, (r.first / tpb) * interval);
+          t += static_cast<double>(weight) * n;
+        }
+        t += overhead;
         load.pop();
         load.push(t);
         span = std::max(span, t);
       }
     }
-    if (ns > 1) span += 4;  // merge pass
+    if (ns > 1) span += ring ? 4 + ns * merge_per_split : 4;  // merge pass
     if (span < best_span * 0.995) {
       best_span = span;
       best = ns;
@@ -194,9 +239,9 @@ FlashPlan flash_plan(const FlashArgs& a) {
   const bool dyn = a.causal && dynamic_enabled();
   if (a.nsplit > 0)
     pl.nsplit = a.nsplit;
-  else if (dyn)
-    pl.nsplit = causal_split(a, a.prec == Prec::kF32x3 ? 64 : 128, pl.rows_per_unit, pl.n_units,
-                             tiles, sms, overhead);
+  else if (dyn || (a.fused && a.nblk > 1))
+    pl.nsplit = simulated_split(a, a.prec == Prec::kF32x3 ? 64 : 128, pl.rows_per_unit,
+                                pl.n_units, tiles, sms, overhead);
   else
     pl.nsplit = flash_choose_split(pl.n_units, tiles, sms, overhead);
   if (pl.nsplit > tiles) pl.nsplit = tiles > 0 ? tiles : 1;

@@ -108,6 +108,30 @@ def test_plan_causal_is_dynamic(C, monkeypatch):
     assert pl["dynamic"] == 1 and pl["nsplit"] == 1
 
 
+def test_plan_fused_causal_follows_ring_blocks(C, monkeypatch):
+    """In a fused ring launch every item walks its chunk's ring blocks in order
+    and waits for each to land; when the blocks arrive slower than the items
+    use them (16k tokens x 32 heads per rank: 268 MB blocks), the causal split
+    cuts the ring at block boundaries so the early items run on the blocks
+    already present.  Long GQA rows use each block for longer than it takes to
+    arrive and keep (nearly) whole items."""
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
+    for world in (2, 4, 8):
+        for rank in (0, world - 1):
+            pl = C.flash_plan_info(BF16, 16384, 16384, world, 32, 32, 128, causal=True,
+                                   zigzag=True, world=world, rank=rank, sms=148, fused=True)
+            ns = pl["nsplit"]
+            assert pl["dynamic"] == 1 and ns >= max(2, world // 2), (world, rank, ns)
+            assert world % ns == 0, (world, rank, ns)  # chunks made of whole ring blocks
+        gqa = C.flash_plan_info(BF16, 65536, 65536, world, 32, 8, 128, causal=True, zigzag=True,
+                                world=world, rank=0, sms=148, fused=True)
+        assert gqa["nsplit"] <= 2, (world, gqa["nsplit"])
+    # the same shape on one GPU (no ring) keeps whole items
+    one = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True, zigzag=True,
+                            sms=148)
+    assert one["nsplit"] == 1
+
+
 def test_plan_forced_modes(C, monkeypatch):
     monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
     pl = C.flash_plan_info(BF16, 4096, 4096, 1, 8, 8, 128, nsplit=-1, sms=148)
