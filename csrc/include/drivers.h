@@ -25,10 +25,12 @@ enum RuntimeFlag : int {
 struct RingCopyParams {
   uint8_t* buf[2];          // this rank's two shard buffers
   uint8_t* right_buf[2];    // the right neighbour's two buffers (peer-mapped)
+  uint8_t* left_buf[2];     // the left neighbour's two buffers (peer-mapped; pull mode)
   uint64_t* arrived_local;  // [slices] written by the left neighbour
   uint64_t* arrived_right;  // the right neighbour's arrived[] (peer-mapped)
   uint64_t* sent_local;     // [slices] this rank's progress
   uint64_t* sent_right;     // the right neighbour's sent[] (peer-mapped)
+  uint64_t* sent_left;      // the left neighbour's sent[] (peer-mapped; pull mode)
   size_t bytes;
   int nsteps;
   int first_step;           // ring step index of this launch's first step (buffer parity)
@@ -36,7 +38,8 @@ struct RingCopyParams {
   DeviceStatus* status;
   uint64_t timeout_ns;
   int mode;                 // 0: 16-byte vector stores, 1: TMA bulk copies through shared
-                            // memory, 2: 32-byte vector loads and stores
+                            // memory, 2: 32-byte vector loads and stores, 3: pull (16-byte
+                            // loads of the left neighbour's buffer, local stores)
 };
 int p2p_ring_launch(const RingCopyParams& p, int slices, cudaStream_t stream);
 
@@ -49,7 +52,8 @@ struct CommOptions {
   int warmup = 10;
   int iters = 100;
   int slices = 0;        // b200_fused CTAs (0: default)
-  int p2p_mode = 0;      // b200_fused copy engine: 0 vector stores, 1 TMA bulk, 2 32-byte vectors
+  int p2p_mode = 0;      // b200_fused copy engine: 0 vector stores, 1 TMA bulk, 2 32-byte vectors,
+                         // 3 pull
   bool precheck = true;
 };
 

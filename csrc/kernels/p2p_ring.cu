@@ -82,7 +82,16 @@ __device__ __forceinline__ void st_vec(Vec32* p, const Vec32& v) {
 }
 
 // Chunks of kVecThreads vectors (8 KiB with 16-byte vectors, 16 KiB with 32-byte ones).
-template <typename V>
+//
+// kPull: the rank reads the left neighbour's buffer over NVLink and writes its
+// own (instead of writing the right neighbour's), and both flags of a step
+// live in the waiting rank's memory, so every poll is a local load:
+//   arrived[c]  bumped by the left neighbour once its buffer holds the data
+//               this rank pulls next (it finished its own previous step)
+//   sent[c]     bumped by the right neighbour once it finished reading the
+//               buffer this rank is about to overwrite
+// The counts match the push protocol's, step for step.
+template <typename V, bool kPull>
 __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyParams p) {
   const int c = blockIdx.x;
   const size_t n16 = p.bytes / sizeof(V);
@@ -94,13 +103,15 @@ __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyPar
     if (threadIdx.x == 0) {
       bool ok = true;
       if (sg > 0) ok = wait_ge(p.arrived_local + c, seq, p.status, (uint32_t)s, p.timeout_ns);
-      if (ok) ok = wait_ge(p.sent_right + c, seq, p.status, 0x10000u | (uint32_t)s, p.timeout_ns);
+      if (ok)
+        ok = wait_ge(kPull ? p.sent_local + c : p.sent_right + c, seq, p.status,
+                     0x10000u | (uint32_t)s, p.timeout_ns);
       s_ok = ok;
     }
     __syncthreads();
     if (!s_ok) return;
-    const V* src = reinterpret_cast<const V*>(p.buf[sg & 1]);
-    V* dst = reinterpret_cast<V*>(p.right_buf[(sg + 1) & 1]);
+    const V* src = reinterpret_cast<const V*>(kPull ? p.left_buf[sg & 1] : p.buf[sg & 1]);
+    V* dst = reinterpret_cast<V*>(kPull ? p.buf[(sg + 1) & 1] : p.right_buf[(sg + 1) & 1]);
     // chunks c, c + G, c + 2G, ... (one vector per thread), kVecUnroll of them
     // in flight; the CTAs' shares differ by one chunk at most
     size_t base = kVecChunk16 * c;
@@ -122,10 +133,17 @@ __global__ void __launch_bounds__(kVecThreads) p2p_ring_kernel(const RingCopyPar
     // measured 9-13 us slower per 64 MiB launch on B200.)
     __syncthreads();
     if (threadIdx.x == 0) {
+      // push: the data landed in the right neighbour's buffer, and this rank
+      // finished reading its own; pull: this rank's buffer holds the right
+      // neighbour's next data, and the left neighbour's buffer was read
       asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.arrived_right + c)
                    : "memory");
-      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.sent_local + c), "l"(seq + 1)
-                   : "memory");
+      if constexpr (kPull)
+        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.sent_left + c)
+                     : "memory");
+      else
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.sent_local + c), "l"(seq + 1)
+                     : "memory");
     }
   }
 }
@@ -260,9 +278,11 @@ int p2p_ring_launch(const RingCopyParams& p, int slices, cudaStream_t stream) {
     if (e != cudaSuccess) return static_cast<int>(e);
     p2p_ring_bulk_kernel<<<slices, 32, smem, stream>>>(p);
   } else if (p.mode == 2 && p.bytes % 32 == 0) {
-    p2p_ring_kernel<Vec32><<<slices, kVecThreads, 0, stream>>>(p);
+    p2p_ring_kernel<Vec32, false><<<slices, kVecThreads, 0, stream>>>(p);
+  } else if (p.mode == 3) {
+    p2p_ring_kernel<uint4, true><<<slices, kVecThreads, 0, stream>>>(p);
   } else {
-    p2p_ring_kernel<uint4><<<slices, kVecThreads, 0, stream>>>(p);
+    p2p_ring_kernel<uint4, false><<<slices, kVecThreads, 0, stream>>>(p);
   }
   return static_cast<int>(cudaGetLastError());
 }

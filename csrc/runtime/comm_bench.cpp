@@ -119,10 +119,13 @@ CommResult run_comm_bench(RingContext& ctx, const CommOptions& o) {
     rp.buf[1] = d2;
     rp.right_buf[0] = ctx.peer(ctx.right(), off1);
     rp.right_buf[1] = ctx.peer(ctx.right(), off2);
+    rp.left_buf[0] = ctx.peer(ctx.left(), off1);
+    rp.left_buf[1] = ctx.peer(ctx.left(), off2);
     rp.arrived_local = ctx.flags_local() + kFlagRingArrived;
     rp.arrived_right = ctx.flags_peer(ctx.right()) + kFlagRingArrived;
     rp.sent_local = ctx.flags_local() + kFlagRingSent;
     rp.sent_right = ctx.flags_peer(ctx.right()) + kFlagRingSent;
+    rp.sent_left = ctx.flags_peer(ctx.left()) + kFlagRingSent;
     rp.bytes = o.bytes;
     rp.status = ctx.status_dev();
     rp.timeout_ns = static_cast<uint64_t>(ctx.host().timeout_s() * 1e9);

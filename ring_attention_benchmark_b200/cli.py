@@ -87,7 +87,8 @@ def _run_comm(rt: RingRuntime, backend: str, kv_size: int, warmup: int, iters: i
     _print(f"[Rank {rt.rank}] KV shard: {kv_size} bytes ({kv_size / 1024.0:.1f} KB), "
            f"neighbors: left={(rt.rank - 1) % rt.world} right={(rt.rank + 1) % rt.world}")
     slices = int(os.environ.get("RAB_P2P_SLICES", "0"))
-    mode = {"vector": 0, "bulk": 1, "vector32": 2}[os.environ.get("RAB_P2P_MODE", "vector")]
+    mode = {"vector": 0, "bulk": 1, "vector32": 2, "pull": 3}[os.environ.get("RAB_P2P_MODE",
+                                                                              "vector")]
     avg = C.run_comm_bench(rt.ctx, backend, kv_size, warmup, iters, slices, True, mode)
     if rt.rank == 0:
         _print(results.comm_result_line(backend, kv_size, rt.world, warmup, iters, avg))

@@ -71,6 +71,12 @@ def case_comm(nbytes):
         avg = C.run_comm_bench(rt.ctx, b, nbytes, 1, 3, 0, True)  # precheck verifies delivery
         if rt.rank == 0:
             print(f"comm {b}: {avg}", flush=True)
+    # every data path of the b200_fused kernel: 16-byte and 32-byte pushes, TMA
+    # bulk pushes, 16-byte pulls (the run ends with a full-content check)
+    for mode in (0, 1, 2, 3):
+        avg = C.run_comm_bench(rt.ctx, "b200_fused", nbytes, 1, 3, 0, True, mode)
+        if rt.rank == 0:
+            print(f"comm b200_fused mode {mode}: {avg}", flush=True)
     rt.close()
 
 

@@ -51,6 +51,7 @@ def test_fused_bf16_two_tile_two_ranks(causal):
 def test_comm_backends_two_ranks():
     out = _run(2, "comm", 1 << 20)
     assert "comm b200_fused" in out
+    assert "comm b200_fused mode 3" in out  # the pull mode delivered the shard too
 
 
 def test_attention_backends_two_ranks():
