@@ -347,7 +347,8 @@ def main() -> int:
                "d2h_bytes_per_step": int(outs_h[0].numel() * outs_h[0].element_size()),
                "output_matches_device_timed_run": ok,
                "schedule": "H2D of step i+1 and D2H of step i-1 overlap step i on two copy "
-                           "streams; K-step loop timed as a whole"}
+                           "streams; K-step loop timed as a whole, steps back to back with no "
+                           "L2 flush or hold between them (each step's inputs arrive by H2D)"}
 
     # ---- output check: sampled rows of every rank vs a float64 recomputation ----
     # over the K/V of ALL ranks, regenerated from their seeds on this GPU (not
