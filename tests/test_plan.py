@@ -130,6 +130,17 @@ def test_plan_fused_causal_follows_ring_blocks(C, monkeypatch):
     one = C.flash_plan_info(BF16, 16384, 16384, 1, 32, 32, 128, causal=True, zigzag=True,
                             sms=148)
     assert one["nsplit"] == 1
+    # without a mask too (two-tile kernel, static item order): block-aligned chunks
+    for world in (4, 8):
+        nc = C.flash_plan_info(BF16, 16384, 16384, world, 32, 32, 128, world=world, sms=148,
+                               fused=True)
+        assert nc["rows_per_unit"] == 256 and nc["balanced"] == 0 and nc["dynamic"] == 0
+        assert nc["nsplit"] >= world // 2 and world % nc["nsplit"] == 0, (world, nc["nsplit"])
+    # the fp32 headline keeps its balanced schedule at every ring size
+    for world in (1, 2, 8):
+        hl = C.flash_plan_info(F32, 16384, 16384, world, 1, 1, 64, world=world, sms=148,
+                               fused=world > 1)
+        assert hl["balanced"] == 1
 
 
 def test_plan_forced_modes(C, monkeypatch):
