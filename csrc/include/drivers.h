@@ -79,8 +79,12 @@ size_t comm_arena_bytes(size_t bytes);
 // ---------------------------------------------------------------------------
 class FusedRing {
  public:
+  // device_epochs: the fused kernel takes its epoch from a call counter in
+  // device memory instead of the launch parameters, so a call's launches are
+  // the same every time and can be captured in a CUDA graph and replayed
+  // (every rank must replay in step: each replay is one ring call).
   FusedRing(RingContext& ctx, Prec prec, int seq, int heads, int heads_kv, int dim, bool causal,
-            bool zigzag, bool ring_chain, double timeout_s);
+            bool zigzag, bool ring_chain, double timeout_s, bool device_epochs = false);
   ~FusedRing();
   FusedRing(const FusedRing&) = delete;
   FusedRing& operator=(const FusedRing&) = delete;
@@ -104,7 +108,8 @@ class FusedRing {
   int nsplit() const { return plan_.balanced ? -1 : plan_.nsplit; }  // -1: balanced schedule
   int merge_launches() const { return plan_.merge_kernel; }  // merge launches per call
   const FlashArgs& args() const { return args_; }  // shapes and precision of the engine
-  uint64_t launches() const { return epoch_; }
+  uint64_t launches() const { return epoch_; }  // attend() calls (a graph replay adds none)
+  bool device_epochs() const { return device_epochs_; }
   // Overlap trace of the following launches (FlashParams::stamps), one
   // [grid][kMaxSlots][2] globaltimer record per launch, cleared before each.
   void set_trace(bool on);
@@ -121,6 +126,7 @@ class FusedRing {
   void* workspace_ = nullptr;
   uint64_t* stamps_ = nullptr;
   bool trace_ = false;
+  bool device_epochs_ = false;
   uint64_t epoch_ = 0;
   uint64_t arrive_total_ = 0;
   uint64_t reads_total_ = 0;

@@ -27,6 +27,8 @@ enum class Prec : int {
 enum FusedFlag : int {
   kFlagSlot0Ready = 0,  // epoch whose slot-0 block is published
   kFlagReads = 1,       // slices of this rank's slots read by peers (cumulative)
+  kFlagCalls = 2,       // device-side epochs: launches completed by this engine
+  kFlagExit = 3,        // device-side epochs: CTAs of the running launch that finished
   kFlagArrivedBase = 8, // + s: slices of slot s landed locally (cumulative)
   kMaxSlots = 64,
 };
@@ -77,6 +79,12 @@ struct FlashParams {
   uint64_t epoch;
   uint64_t arrive_target;  // value of flag kFlagArrivedBase+s once this launch copied slot s
   uint64_t reads_target;   // value of kFlagReads once every peer finished this launch's reads
+  // Device-side epochs (nullptr: epoch and targets above, set by the host per
+  // launch): this launch's epoch is *call_counter + 1, the targets follow from
+  // it and the grid, and the launch's last CTA to finish bumps the counter, so
+  // the launch parameters stay the same from call to call (a captured CUDA
+  // graph can replay them).  Points at flag word kFlagCalls; kFlagExit follows.
+  uint64_t* call_counter;
   // ---- diagnostics ----
   DeviceStatus* status;
   uint64_t timeout_ns;
@@ -182,6 +190,7 @@ struct FlashArgs {
   uint64_t epoch = 0;
   uint64_t arrive_target = 0;
   uint64_t reads_target = 0;
+  uint64_t* call_counter = nullptr;  // device-side epochs (FlashParams::call_counter)
   uint64_t* stamps = nullptr;        // optional overlap trace (FlashParams::stamps)
 };
 

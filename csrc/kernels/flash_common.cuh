@@ -273,11 +273,40 @@ __device__ __forceinline__ void trace_stamp(const FlashParams& p, int slot, int 
     p.stamps[(static_cast<size_t>(blockIdx.x) * kMaxSlots + slot) * 2 + which] = t;
 }
 
+// Epoch of this launch and the cumulative flag values it waits for: from the
+// launch parameters, or (device-side epochs) from the engine's call counter,
+// which only the previous launch's last CTA wrote.  Every launch of an engine
+// has the same grid: each CTA adds one slice per ring block to the arrival
+// flags, and every peer reads one slice per CTA of this rank's slot 0.
+struct RingTargets {
+  uint64_t epoch, arrive, reads;
+};
+
+__device__ __forceinline__ RingTargets ring_targets(const FlashParams& p) {
+  if (p.call_counter == nullptr) return {p.epoch, p.arrive_target, p.reads_target};
+  const uint64_t e = *reinterpret_cast<volatile const uint64_t*>(p.call_counter) + 1;
+  return {e, e * gridDim.x, e * static_cast<uint64_t>(p.world - 1) * gridDim.x};
+}
+
+// Device-side epochs: called by one thread of every CTA after the CTA's last
+// use of the epoch; the last CTA of the launch to get here bumps the call
+// counter for the next launch and clears the exit count.
+__device__ __forceinline__ void finish_launch(const FlashParams& p) {
+  if (p.call_counter == nullptr) return;
+  unsigned long long* exits = reinterpret_cast<unsigned long long*>(p.call_counter + 1);
+  __threadfence();
+  if (atomicAdd(exits, 1ull) == gridDim.x - 1) {
+    atomicExch(exits, 0ull);
+    atomicAdd(reinterpret_cast<unsigned long long*>(p.call_counter), 1ull);
+    __threadfence();
+  }
+}
+
 // The TMA thread's wait for ring block s to be present locally (fused mode),
 // with the overlap trace.
 __device__ __forceinline__ bool wait_block(const FlashParams& p, int s) {
   const uint64_t t0 = p.stamps != nullptr ? globaltimer_ns() : 0;
-  const bool ok = wait_flag(p.flags_local + kFlagArrivedBase + s, p.arrive_target, false,
+  const bool ok = wait_flag(p.flags_local + kFlagArrivedBase + s, ring_targets(p).arrive, false,
                             p.status, kSiteBlockReady, s, p.timeout_ns);
   if (p.stamps != nullptr) {
     trace_stamp(p, s, 0, t0);
@@ -298,7 +327,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __device__ __forceinline__ void ring_copy_role(const FlashParams& p, int ct, int* s_copy_ok) {
   DeviceStatus* st = p.status;
   const uint64_t tmo = p.timeout_ns;
-  if (blockIdx.x == 0 && ct == 0) st_release_sys(p.flags_local + kFlagSlot0Ready, p.epoch);
+  const RingTargets tg = ring_targets(p);
+  if (blockIdx.x == 0 && ct == 0) st_release_sys(p.flags_local + kFlagSlot0Ready, tg.epoch);
   const int left = (p.rank - 1 + p.world) % p.world;
   const size_t n16 = p.slot_bytes / 16;
   const size_t per = (n16 + gridDim.x - 1) / gridDim.x;
@@ -319,10 +349,10 @@ __device__ __forceinline__ void ring_copy_role(const FlashParams& p, int ct, int
     if (ct == 0) {
       bool w;
       if (p.ring_chain && s > 1)
-        w = wait_flag(src_flags + kFlagArrivedBase + (s - 1), p.arrive_target, true, st,
+        w = wait_flag(src_flags + kFlagArrivedBase + (s - 1), tg.arrive, true, st,
                       kSitePeerReady, s, tmo);
       else
-        w = wait_flag(src_flags + kFlagSlot0Ready, p.epoch, true, st, kSitePeerReady, s, tmo);
+        w = wait_flag(src_flags + kFlagSlot0Ready, tg.epoch, true, st, kSitePeerReady, s, tmo);
       *s_copy_ok = (w && st_read_error(st) == 0) ? 1 : 0;
     }
     named_bar_sync(1, 64);
@@ -349,7 +379,7 @@ __device__ __forceinline__ void ring_copy_role(const FlashParams& p, int ct, int
   }
   // this rank's slots must outlive every peer's reads of this launch
   if (ok && blockIdx.x == 0 && ct == 0)
-    wait_flag(p.flags_local + kFlagReads, p.reads_target, true, st, kSitePeerConsumed, 0, tmo);
+    wait_flag(p.flags_local + kFlagReads, tg.reads, true, st, kSitePeerConsumed, 0, tmo);
 }
 
 }  // namespace flash_detail

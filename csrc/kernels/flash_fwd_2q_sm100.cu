@@ -600,6 +600,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       atomicExch(&st->pad[1], 0u);
     }
   }
+  if (threadIdx.x == 0) finish_launch(p);  // device-side epochs: bump the call counter
   if (warp == kWMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kCols);

@@ -618,6 +618,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsP, 1)
       atomicExch(&st->pad[1], 0u);
     }
   }
+  if (threadIdx.x == 0) finish_launch(p);  // device-side epochs: bump the call counter
   // neither CTA leaves (or frees TMEM) while the pair's MMAs or the peer's
   // remote arrivals can still touch it
   cluster_sync();

@@ -674,6 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicExch(&st->pad[1], 0u);
     }
   }
+  if (threadIdx.x == 0) finish_launch(p);  // device-side epochs: bump the call counter
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

@@ -313,6 +313,7 @@ int flash_run(const FlashArgs& a, const FlashPlan& pl, cudaStream_t stream) {
   p.epoch = a.epoch;
   p.arrive_target = a.arrive_target;
   p.reads_target = a.reads_target;
+  p.call_counter = a.fused ? a.call_counter : nullptr;
   p.status = a.status;
   p.timeout_ns = static_cast<uint64_t>(a.timeout_s * 1e9);
   p.stamps = a.stamps;

@@ -16,8 +16,9 @@ size_t FusedRing::arena_bytes(Prec prec, int seq, int heads_kv, int dim, int wor
 }
 
 FusedRing::FusedRing(RingContext& ctx, Prec prec, int seq, int heads, int heads_kv, int dim,
-                     bool causal, bool zigzag, bool ring_chain, double timeout_s)
-    : ctx_(ctx) {
+                     bool causal, bool zigzag, bool ring_chain, double timeout_s,
+                     bool device_epochs)
+    : ctx_(ctx), device_epochs_(device_epochs) {
   const int np = ctx.world();
   if (np > kMaxSlots) throw std::runtime_error("FusedRing: too many ranks");
   if (np > 1 && !ctx.peers_open())
@@ -25,7 +26,8 @@ FusedRing::FusedRing(RingContext& ctx, Prec prec, int seq, int heads, int heads_
   if (np > 1 && !ctx.devices_unique())
     throw std::runtime_error(
         "FusedRing: ranks spin on each other inside the kernel and need one GPU each");
-  // the flag words count launches of this engine from zero on every rank
+  // the flag words (and, with device-side epochs, the call counter) count
+  // launches of this engine from zero on every rank
   ctx.reset_flags();
   slot_bytes_ = ring_block_bytes(prec, seq, heads_kv, dim);
   slots_off_ = ctx.arena_alloc(static_cast<size_t>(np) * slot_bytes_, 4096);
@@ -101,8 +103,11 @@ void FusedRing::attend(const void* q, void* out, bool out_bf16, float* lse, floa
   a.out_bf16 = out_bf16;
   a.lse = lse;
   a.scale = scale;
-  if (a.fused) {
-    ++epoch_;
+  ++epoch_;
+  if (a.fused && device_epochs_) {
+    // the kernel reads its epoch from the call counter (flag word kFlagCalls)
+    a.call_counter = ctx_.flags_local() + kFlagCalls;
+  } else if (a.fused) {
     arrive_total_ += static_cast<uint64_t>(plan_.grid);
     reads_total_ += static_cast<uint64_t>(a.world - 1) * plan_.grid;
     a.epoch = epoch_;

@@ -233,14 +233,16 @@ void register_runtime(py::module_& m) {
 
   py::class_<FusedRing>(m, "FusedRing")
       .def(py::init([](RingContext& ctx, const std::string& prec, int seq, int heads, int heads_kv,
-                       int dim, bool causal, bool zigzag, bool ring_chain, double timeout_s) {
+                       int dim, bool causal, bool zigzag, bool ring_chain, double timeout_s,
+                       bool device_epochs) {
              return std::make_unique<FusedRing>(ctx, prec_from(prec), seq, heads, heads_kv, dim,
-                                                causal, zigzag, ring_chain, timeout_s);
+                                                causal, zigzag, ring_chain, timeout_s,
+                                                device_epochs);
            }),
            py::arg("ctx"), py::arg("prec"), py::arg("seq"), py::arg("heads"),
            py::arg("heads_kv"), py::arg("dim"), py::arg("causal") = false,
            py::arg("zigzag") = false, py::arg("ring_chain") = false,
-           py::arg("timeout_s") = 10.0, py::keep_alive<1, 2>())
+           py::arg("timeout_s") = 10.0, py::arg("device_epochs") = false, py::keep_alive<1, 2>())
       .def_static("arena_bytes", [](const std::string& prec, int seq, int heads_kv, int dim,
                                     int world) {
         return FusedRing::arena_bytes(prec_from(prec), seq, heads_kv, dim, world);
@@ -286,6 +288,7 @@ void register_runtime(py::module_& m) {
       .def_property_readonly("nsplit", &FusedRing::nsplit)
       .def_property_readonly("merge_launches", &FusedRing::merge_launches)
       .def_property_readonly("launches", &FusedRing::launches)
+      .def_property_readonly("device_epochs", &FusedRing::device_epochs)
       .def("slot0_ptrs", [](FusedRing& f) {
         return std::make_pair(reinterpret_cast<uintptr_t>(f.slot0_k()),
                               reinterpret_cast<uintptr_t>(f.slot0_v()));

@@ -23,6 +23,14 @@ blocks that are present, and the online-softmax state never leaves the chip.
 The engine allocates its ring slots once (``world`` blocks in the symmetric,
 IPC-mapped arena).  Writing K and V straight into slot 0 (``kv_slot()``) skips
 the per-call copy for bf16 inputs.
+
+CUDA graphs: a call is a fixed sequence of launches on the current stream, but
+with more than one rank the fused kernel's launch parameters carry the call's
+epoch (the flag values it waits for).  ``graph_safe=True`` moves the epoch into
+a call counter in device memory that the kernel itself advances, so a call
+captured once (``capture()``, or any ``torch.cuda.graph`` region) can be
+replayed; every rank must capture and replay in step, one replay being one
+ring call, with the same input and output tensors each time.
 """
 from __future__ import annotations
 
@@ -40,7 +48,8 @@ class RingAttention:
     def __init__(self, seq_per_rank: int, heads: int = 1, head_dim: int = 64,
                  heads_kv: Optional[int] = None, dtype: torch.dtype = torch.float32,
                  causal: bool = False, zigzag: Optional[bool] = None, ring_mode: str = "direct",
-                 runtime: Optional[RingRuntime] = None, timeout_s: float = 10.0):
+                 runtime: Optional[RingRuntime] = None, timeout_s: float = 10.0,
+                 graph_safe: bool = False):
         if dtype not in _DTYPES:
             raise ValueError("dtype must be torch.float32 or torch.bfloat16")
         if ring_mode not in ("direct", "chain"):
@@ -63,7 +72,9 @@ class RingAttention:
                                                           head_dim, world))
         self.runtime = runtime
         self.engine = C.FusedRing(runtime.ctx, prec, seq_per_rank, heads, self.heads_kv, head_dim,
-                                  causal, self.zigzag, ring_mode == "chain", timeout_s)
+                                  causal, self.zigzag, ring_mode == "chain", timeout_s,
+                                  graph_safe)
+        self.graph_safe = graph_safe
         # the per-call checks compare against these (built once: a call's host
         # path is on the critical path of a step that starts from an idle GPU)
         self._dev = torch.device("cuda", runtime.device)
@@ -140,6 +151,26 @@ class RingAttention:
         finally:
             self.engine.set_trace(False)
         return summarize(stamps, self.world)
+
+    def capture(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: Optional[torch.Tensor] = None, scale: Optional[float] = None):
+        """Capture one call into a CUDA graph and return ``(graph, out)``:
+        ``graph.replay()`` reruns the whole ring call on the same ``q``, ``k``,
+        ``v`` (refill them in place between replays) into ``out``.  Needs
+        ``graph_safe=True`` when the ring has more than one rank; every rank
+        captures together and replays in step.  Runs one eager call first (it
+        loads the kernels and sets their attributes outside the capture)."""
+        if self.world > 1 and not self.graph_safe:
+            raise RuntimeError("capture() with more than one rank needs "
+                               "RingAttention(..., graph_safe=True)")
+        if out is None:
+            out = torch.empty_like(q)
+        self(q, k, v, scale=scale, out=out, check=True)  # eager warm-up call
+        torch.cuda.synchronize(q.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self(q, k, v, scale=scale, out=out)
+        return graph, out
 
     def close(self) -> None:
         self.engine = None

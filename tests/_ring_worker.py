@@ -62,6 +62,48 @@ def case_fused(dtype_name, causal, hq, hk, d, spr, mode):
     print(f"rank {rank}: fused ok err={err:.2e}", flush=True)
 
 
+def case_graph(dtype_name, causal, hq, hk, d, spr):
+    """Device-side epochs: one call captured into a CUDA graph on every rank,
+    then replayed in step with fresh inputs written into the captured tensors;
+    each replay checked against the float64 oracle (and, in between, an eager
+    call on the same engine keeps the call counter in step)."""
+    dtype = torch.float32 if dtype_name == "fp32" else torch.bfloat16
+    info = detect_ranks()
+    world, rank = info.world, info.rank
+    scale = d ** -0.5
+    attn = RingAttention(spr, hq, d, heads_kv=hk, dtype=dtype, causal=causal, graph_safe=True)
+    dev = torch.device("cuda", attn.runtime.device)
+    qs, ks, vs, pos = all_inputs(world, spr, hq, hk, d, dtype, causal)
+    q, k, v = qs[rank].to(dev), ks[rank].to(dev), vs[rank].to(dev)
+    graph, out = attn.capture(q, k, v)
+    tol = 2e-5 if dtype == torch.float32 else 2e-2
+    for rep in range(3):
+        g = torch.Generator().manual_seed(100 + rep)
+        total = world * spr
+        glob = [torch.randn(total, hq, d, generator=g) * 0.5,
+                torch.randn(total, hk, d, generator=g) * 0.5,
+                torch.randn(total, hk, d, generator=g) * 0.5]
+        if causal:
+            sh = [[oracle.zigzag_shard(t, r, world).to(dtype) for t in glob] for r in range(world)]
+        else:
+            sh = [[t.chunk(world)[r].to(dtype).contiguous() for t in glob] for r in range(world)]
+        for dst, src in zip((q, k, v), sh[rank]):
+            dst.copy_(src)
+        graph.replay()
+        if rep == 1:  # an eager call between replays advances the same counter
+            attn(q, k, v, check=True)
+        torch.cuda.synchronize(dev)
+        attn.check()
+        ref = oracle.ring_attention([s[0].double() for s in sh], [s[1].double() for s in sh],
+                                    [s[2].double() for s in sh], scale, pos)[rank]
+        err = (out.double().cpu() - ref).abs().max().item()
+        if not err < tol:
+            raise SystemExit(f"rank {rank}: graph replay {rep} err {err} > {tol}")
+    del graph
+    attn.close()
+    print(f"rank {rank}: graph ok", flush=True)
+
+
 def case_comm(nbytes):
     C = _ext.load()
     info = detect_ranks()
@@ -113,6 +155,9 @@ if __name__ == "__main__":
     if c == "fused":
         case_fused(sys.argv[2], sys.argv[3] == "1", int(sys.argv[4]), int(sys.argv[5]),
                    int(sys.argv[6]), int(sys.argv[7]), sys.argv[8])
+    elif c == "graph":
+        case_graph(sys.argv[2], sys.argv[3] == "1", int(sys.argv[4]), int(sys.argv[5]),
+                   int(sys.argv[6]), int(sys.argv[7]))
     elif c == "comm":
         case_comm(int(sys.argv[2]))
     elif c == "attn":

@@ -48,6 +48,15 @@ def test_fused_bf16_two_tile_two_ranks(causal):
     _run(2, "fused", "bf16", causal, 8, 2, 128, 1024, "direct", extra_env={"RAB_FLASH_2Q": "1"})
 
 
+@pytest.mark.parametrize("dtype,causal", [("fp32", 0), ("bf16", 1)])
+def test_graph_replay_two_ranks(dtype, causal):
+    """graph_safe=True: each rank captures one fused ring call into a CUDA
+    graph and the ranks replay it in step (the kernel takes its epoch from a
+    device-side call counter instead of its launch parameters)."""
+    d = 64 if dtype == "fp32" else 128
+    _run(2, "graph", dtype, causal, 4, 2, d, 512)
+
+
 def test_comm_backends_two_ranks():
     out = _run(2, "comm", 1 << 20)
     assert "comm b200_fused" in out
