@@ -144,7 +144,8 @@ def load_records(path: str) -> List[Dict]:
 
 def sweep_table(records: List[Dict], kind: str) -> str:
     """Markdown table of a sweep's records: one row per (ranks, backend), one
-    column per size.  comm: total GB/s ((np-1) * bytes / avg_total); attention:
+    column per size.  comm: total GB/s ((np-1) * bytes / avg_total), and for
+    the b200_fused kernel its device-timed GB/s in brackets; attention:
     avg_total ms and TFLOP/s.  The last record of a configuration wins."""
     cells: Dict = {}
     sizes, rows = set(), []
@@ -158,14 +159,19 @@ def sweep_table(records: List[Dict], kind: str) -> str:
         total = r["avg_ms"].get("total", 0.0)
         if kind == "comm":
             g = gbps((r["ranks"] - 1) * r["bytes"], total)
-            cells[key + (r["bytes"],)] = "n/a" if g is None else f"{g:.1f}"
+            cell = "n/a" if g is None else f"{g:.1f}"
+            kg = gbps((r["ranks"] - 1) * r["bytes"], r["avg_ms"].get("kernel", 0.0))
+            if kg is not None and r["avg_ms"].get("kernel", 0.0) > 0:
+                cell += f" ({kg:.1f})"
+            cells[key + (r["bytes"],)] = cell
         else:
             cells[key + (r["bytes"],)] = f"{total:.3f} ms / {r.get('tflops', 0.0):.2f}"
     cols = sorted(sizes)
     unit = "bytes" if kind == "comm" else "bytes (tokens/rank = bytes/256)"
     head = "| np | backend | " + " | ".join(str(c) for c in cols) + " |"
     lines = [f"({kind}; columns: shard size in {unit}; cells: "
-             + ("total GB/s" if kind == "comm" else "avg_total ms / TFLOP/s") + ")", "",
+             + ("total GB/s (kernel GB/s)" if kind == "comm" else "avg_total ms / TFLOP/s")
+             + ")", "",
              head, "|" + "---|" * (len(cols) + 2)]
     for key in sorted(rows, key=lambda k: (k[0], rows.index(k))):
         lines.append(f"| {key[0]} | {key[1]} | " +

@@ -210,14 +210,14 @@ def test_sweep_table_from_jsonl():
     recs = [{"kind": "comm", "backend": "nccl", "bytes": 1 << 20, "ranks": 2,
              "avg_ms": {"total": 0.01}},
             {"kind": "comm", "backend": "b200_fused", "bytes": 1 << 20, "ranks": 2,
-             "avg_ms": {"total": 0.005}},
+             "avg_ms": {"total": 0.005, "kernel": 0.004}},
             {"kind": "comm", "backend": "nccl", "bytes": 1 << 24, "ranks": 4,
              "avg_ms": {"total": 0.1}},
             {"kind": "attention", "backend": "nccl", "bytes": 262144, "ranks": 2,
              "avg_ms": {"total": 0.5}, "tflops": 1.2}]
     t = sweep_table(recs, "comm").splitlines()
     assert "| np | backend | 1048576 | 16777216 |" in t
-    assert "| 2 | b200_fused | 209.7 |  |" in t
+    assert "| 2 | b200_fused | 209.7 (262.1) |  |" in t  # device-timed kernel GB/s in brackets
     assert "| 4 | nccl |  | 503.3 |" in t
     assert "| 2 | nccl | 0.500 ms / 1.20 |" in sweep_table(recs, "attention")
 
