@@ -174,3 +174,33 @@ def test_pair_kernel_plan(monkeypatch):
                              sms=148)["rows_per_unit"] != 512
     monkeypatch.setenv("RAB_FLASH_2SM", "0")
     assert C.flash_plan_info(0, 4096, 4096, 1, 8, 8, 128, sms=148)["rows_per_unit"] != 512
+
+
+def test_plan_split_invariants(C, monkeypatch):
+    """Whatever split the planner picks, the plan is self-consistent: items =
+    units x split, the grid never exceeds the SMs (fused launches use every SM,
+    each CTA also copies a slice), the split never exceeds the tiles of a unit,
+    and the workspace holds one partial record per item when there is a split."""
+    monkeypatch.delenv("RAB_FLASH_2Q", raising=False)
+    for prec, d in ((BF16, 128), (BF16, 64), (F32, 64)):
+        for causal in (False, True):
+            for world in (1, 2, 3, 8):
+                for seq, heads in ((1024, 4), (4096, 8), (16384, 1)):
+                    pl = C.flash_plan_info(prec, seq, seq, world, heads, heads, d, causal=causal,
+                                           zigzag=causal, world=world, rank=world - 1, sms=148,
+                                           fused=world > 1)
+                    kn = 64 if prec == F32 else 128
+                    tiles = world * seq // kn
+                    assert 1 <= pl["grid"] <= 148
+                    if pl["balanced"]:
+                        assert pl["n_items"] == pl["grid"] and not causal
+                        continue
+                    ns = pl["nsplit"]
+                    assert 1 <= ns <= max(1, tiles), pl
+                    assert pl["n_items"] == pl["n_units"] * ns
+                    assert pl["n_units"] == heads * seq // pl["rows_per_unit"]
+                    if world > 1:
+                        assert pl["grid"] == 148
+                    rec = pl["n_items"] * pl["rows_per_unit"] * (d + 2) * 4
+                    assert pl["workspace_bytes"] == (rec if ns > 1 else 0)
+                    assert pl["merge_kernel"] == (1 if ns > 1 else 0)
