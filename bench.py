@@ -49,7 +49,8 @@ HOLD_CYCLES = 1_000_000  # device-side hold before each timed step: ~0.5 ms at 1
 # name: (tokens per rank, q heads, kv heads, head dim, dtype, causal, input scale, seed)
 PRESETS = {
     # the reference's full ring attention at its largest ATTENTION_SIZES entry
-    # (config.example.env:31: 1048576 bytes = 16384 fp32 tokens x d=64; headline)
+    # (config.example.env:31) read as fp32 elements: 1048576 elements = 16384
+    # tokens x d=64 per rank, 4194304 bytes on the reference's command line
     "ref-fp32": (16384, 1, 1, 64, "fp32", False, 1.0, None),
     # multi-head bf16, causal with zigzag sharding
     "mha-bf16-causal": (16384, 32, 32, 128, "bf16", True, 1.0, None),
